@@ -1,0 +1,135 @@
+"""Torch-tensor front of the C ABI: output/workspace allocation, pointer and stream passing.
+
+PyTorch is used only as the owner of device memory and of the current CUDA stream; every
+computation below runs in libcfk_b200.so.  Tensors must live on a CUDA device: there is no CPU path.
+"""
+import ctypes
+
+import torch
+
+from colabfold_kernels import _lib
+
+_TAGS = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float8_e4m3fn: _lib.E4M3}
+
+
+def tag(dtype):
+  try:
+    return _TAGS[dtype]
+  except KeyError:
+    raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def _ptr(t):
+  if t is None:
+    return None
+  if not t.is_cuda:
+    raise ValueError("colabfold_kernels (B200) takes CUDA tensors only: there is no CPU fallback")
+  return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+  return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _c(t):
+  return None if t is None else t.contiguous()
+
+
+def device_status(reset=True):
+  """The per-device word kernels set when a bounded wait ran out (0 = clean)."""
+  return _lib.load().cfk_last_device_status(int(reset))
+
+
+# ------------------------------------------------------------------------------------------ LayerNorm
+def layer_norm(x, scale, offset, eps=1e-5):
+  x = _c(x)
+  c = x.shape[-1]
+  y = torch.empty_like(x)
+  m = x.numel() // c
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_layer_norm", _ptr(x), _ptr(_c(scale.float())), _ptr(_c(offset.float())), _ptr(y), m, c,
+              tag(x.dtype), float(eps), _stream())
+  return y
+
+
+def layer_norm_bwd(x, scale, dy, eps=1e-5):
+  x, dy = _c(x), _c(dy.to(x.dtype))
+  c = x.shape[-1]
+  m = x.numel() // c
+  dx = torch.empty_like(x)
+  dscale = torch.empty(c, dtype=torch.float32, device=x.device)
+  doffset = torch.empty(c, dtype=torch.float32, device=x.device)
+  with torch.cuda.device(x.device):
+    nbytes = _lib.load().cfk_layer_norm_bwd_workspace_bytes(m, c)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _lib.call("cfk_layer_norm_bwd", _ptr(x), _ptr(_c(scale.float())), _ptr(dy), _ptr(dx), _ptr(dscale), _ptr(doffset),
+              m, c, tag(x.dtype), float(eps), _ptr(ws), nbytes, _stream())
+  return dx, dscale, doffset
+
+
+# ------------------------------------------------------------------------------------------ attention
+def attention_fwd(q, k, v, bias, kmask, scale, seq_major=False, want_lse=False):
+  """q/k/v [n,h,s,d] (or [n,s,h,d]); bias [h,sq,sk] or None; kmask [n,sk] bool/uint8 -> out (, lse [n,h,sq])."""
+  q, k, v = _c(q), _c(k), _c(v)
+  if seq_major:
+    n, sq, h, d = q.shape
+    sk = k.shape[1]
+  else:
+    n, h, sq, d = q.shape
+    sk = k.shape[2]
+  bias = None if bias is None else _c(bias.to(q.dtype))
+  km = _c(kmask.to(torch.uint8))
+  out = torch.empty_like(q)
+  lse = torch.empty((n, h, sq), dtype=torch.float32, device=q.device) if want_lse else None
+  with torch.cuda.device(q.device):
+    _lib.call("cfk_attention_fwd", _ptr(q), _ptr(k), _ptr(v), _ptr(bias), _ptr(km), _ptr(out), _ptr(lse), n, h, sq, sk,
+              d, tag(q.dtype), int(seq_major), float(scale), _stream())
+  return (out, lse) if want_lse else out
+
+
+def attention_bwd(q, k, v, bias, kmask, out, dout, lse, scale, seq_major=False, want_dbias=True):
+  """-> dq, dk, dv, dbias [h,sq,sk] fp32 (None when not wanted)."""
+  q, k, v, out = _c(q), _c(k), _c(v), _c(out)
+  dout = _c(dout.to(q.dtype))
+  if seq_major:
+    n, sq, h, d = q.shape
+    sk = k.shape[1]
+  else:
+    n, h, sq, d = q.shape
+    sk = k.shape[2]
+  bias = None if bias is None else _c(bias.to(q.dtype))
+  km = _c(kmask.to(torch.uint8))
+  dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+  dbias = torch.empty((h, sq, sk), dtype=torch.float32, device=q.device) if want_dbias else None
+  with torch.cuda.device(q.device):
+    nbytes = _lib.load().cfk_attention_bwd_workspace_bytes(n, h, sq, sk, d, tag(q.dtype))
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    _lib.call("cfk_attention_bwd", _ptr(q), _ptr(k), _ptr(v), _ptr(bias), _ptr(km), _ptr(out), _ptr(dout),
+              _ptr(_c(lse)), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dbias), n, h, sq, sk, d, tag(q.dtype),
+              int(seq_major), float(scale), _ptr(ws), nbytes, _stream())
+  return dq, dk, dv, dbias
+
+
+def trim_limits(kmask):
+  km = _c(kmask.to(torch.uint8))
+  lim = torch.empty(km.shape[0] + 1, dtype=torch.int32, device=km.device)
+  with torch.cuda.device(km.device):
+    _lib.call("cfk_trim_limits", _ptr(km), _ptr(lim), km.shape[0], km.shape[1], _stream())
+  return lim
+
+
+def packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=False, trim=False, want_lse=False):
+  """p [X,Y,G,H,D] -> out [X,Y,H,D] (, lse [batch,H,S])."""
+  p = _c(p)
+  x, y, g, h, d = p.shape
+  nb, s = (y, x) if column else (x, y)
+  bias = None if bias is None else _c(bias.to(p.dtype))
+  gb = None if gate_bias is None else _c(gate_bias.to(p.dtype))
+  km = _c(kmask.to(torch.uint8))
+  out = torch.empty((x, y, h, d), dtype=p.dtype, device=p.device)
+  lse = torch.empty((nb, h, s), dtype=torch.float32, device=p.device) if want_lse else None
+  lim = trim_limits(km) if trim else None
+  with torch.cuda.device(p.device):
+    _lib.call("cfk_packed_attention_fwd", _ptr(p), _ptr(bias), _ptr(km), _ptr(gb), _ptr(out), _ptr(lse), _ptr(lim),
+              x, y, g, h, d, tag(p.dtype), int(column), float(sm_scale), _stream())
+  return (out, lse) if want_lse else out

@@ -1,0 +1,101 @@
+/* C ABI of libcfk_b200.so: the B200 (sm_100a) kernels behind colabfold-kernels' Evoformer hot path.
+ *
+ * Conventions (modelled on the reference's own native FFI, src/colabfold_kernels/volta.py:100-461 and
+ * contract.py:48-53): every pointer is DEVICE memory owned by the caller; entry points neither allocate
+ * nor free (scratch is a caller buffer sized by the matching *_workspace_bytes query, as the reference
+ * requests scratch as an extra output, contract.py:16-17); work is enqueued on `stream` (a cudaStream_t)
+ * without host synchronisation; absent optional tensors are NULL.  Every function returns CFK_OK or a
+ * negative status and never throws or aborts.  dtype tags: CFK_F32, CFK_BF16, CFK_E4M3.
+ *
+ * Citations name the reference interface each entry replaces (paths inside mirditalab/colabfold-kernels).
+ */
+#ifndef CFK_B200_H_
+#define CFK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CFK_API __attribute__((visibility("default")))
+#else
+#define CFK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  CFK_OK = 0,
+  CFK_ERR_SHAPE = -1,       /* a size is zero/negative or outside what the kernel takes */
+  CFK_ERR_DTYPE = -2,       /* dtype tag not supported by this entry */
+  CFK_ERR_ALIGN = -3,       /* a pointer or stride is not 16-byte aligned where TMA / vector loads need it */
+  CFK_ERR_NULL = -4,        /* a required pointer is NULL */
+  CFK_ERR_WORKSPACE = -5,   /* workspace too small */
+  CFK_ERR_LAUNCH = -6,      /* the CUDA runtime refused the launch */
+  CFK_ERR_TMA = -7,         /* tensor-map encoding failed */
+  CFK_ERR_UNSUPPORTED = -8, /* valid request this build has no kernel for (caller runs its own path) */
+  CFK_ERR_DEVICE_WAIT = -9  /* a bounded device-side wait ran out (cfk_last_device_status) */
+};
+
+enum { CFK_F32 = 0, CFK_BF16 = 1, CFK_E4M3 = 2 };
+
+/* Library identification string. */
+CFK_API const char* cfk_version(void);
+
+/* Reads (and optionally clears) the per-device status word that kernels set when one of their bounded
+ * waits ran out: 0 = clean.  Synchronises the device.  No reference counterpart (the reference's
+ * handlers report through XLA's FFI error object). */
+CFK_API int cfk_last_device_status(int reset);
+
+/* ---- LayerNorm ------------------------------------------------------------------------------------
+ * y = (x - mean) * rsqrt(var + eps) * scale + offset over the last axis, fp32 statistics.
+ * x, y [m, c] in `dtype` (CFK_BF16 or CFK_F32); scale, offset [c] fp32.
+ * Replaces pallas_layer_norm, tri_mul.py:492-512 (FFI shape: volta.py:223-229). */
+CFK_API int cfk_layer_norm(const void* x, const float* scale, const float* offset, void* y, int64_t m, int c, int dtype,
+                   float eps, void* stream);
+
+/* LayerNorm backward, grads.py:25-39: dx [m,c] in `dtype`; dscale, doffset [c] fp32 (overwritten).
+ * workspace: cfk_layer_norm_bwd_workspace_bytes(m, c) bytes. */
+CFK_API size_t cfk_layer_norm_bwd_workspace_bytes(int64_t m, int c);
+CFK_API int cfk_layer_norm_bwd(const void* x, const float* scale, const void* dy, void* dx, float* dscale, float* doffset,
+                       int64_t m, int c, int dtype, float eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Bias-fused attention ---------------------------------------------------------------------------
+ * out = softmax_k(scale * q.k + bias[h,q,k], masked keys -> finite floor) . v, per (batch n, head h).
+ * q [n,h,sq,d] ('heads') or [n,sq,h,d] (seq_major); k, v likewise with sk; bias [h,sq,sk] in `dtype` or NULL;
+ * kmask [n,sk] uint8 (0 = masked); out in q's layout and dtype; lse [n,h,sq] fp32 (log2 domain) or NULL.
+ * dtype CFK_BF16 (tcgen05 path when d is 16/32/64 and sk % 8 == 0, else the fp32-math path) or CFK_F32.
+ * Replaces tri_flash / pallas_attention's kernel call, tri_flash.py:242-290,452-478 (FFI: volta.py:100-115). */
+CFK_API int cfk_attention_fwd(const void* q, const void* k, const void* v, const void* bias, const uint8_t* kmask, void* out,
+                      float* lse, int n, int h, int sq, int sk, int d, int dtype, int seq_major, float scale,
+                      void* stream);
+
+/* Backward of the above: tri_flash_bwd, tri_flash.py:365-413,434-446 (FFI: volta.py:118-130).
+ * dq, dk, dv in `dtype` and q/k/v's layout; dbias [h,sq,sk] fp32 or NULL (not wanted).
+ * workspace: cfk_attention_bwd_workspace_bytes(...) bytes, contents undefined on return. */
+CFK_API size_t cfk_attention_bwd_workspace_bytes(int n, int h, int sq, int sk, int d, int dtype);
+CFK_API int cfk_attention_bwd(const void* q, const void* k, const void* v, const void* bias, const uint8_t* kmask,
+                      const void* out, const void* dout, const float* lse, void* dq, void* dk, void* dv, float* dbias,
+                      int n, int h, int sq, int sk, int d, int dtype, int seq_major, float scale, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Attention reading q/k/v/gate in place from the packed projection p [X,Y,G,H,D] (slots q,k,v[,gate]):
+ * rows attend along Y (batch X), columns along X (batch Y); out [X,Y,H,D] = o * sigmoid(gate + gate_bias[h,:])
+ * when G == 4.  bias [H,S,S] or NULL; kmask [batch,S] uint8; gate_bias [H,D] in `dtype` (G == 4) or NULL.
+ * trim_limits (NULL = off): int32 [batch + 1] from cfk_trim_limits; rows with no live key and queries past
+ * the last live key of any row then give zeros (packed_attn.py:123-137).  lse [batch,H,S] fp32 or NULL.
+ * Replaces packed_attention, packed_attn.py:26-120 (FFI: volta.py:200-220, where the limits are likewise
+ * one extra int32 input). */
+CFK_API int cfk_packed_attention_fwd(const void* p, const void* bias, const uint8_t* kmask, const void* gate_bias, void* out,
+                             float* lse, const int32_t* trim_limits, int x, int y, int g, int h, int d, int dtype,
+                             int column, float scale, void* stream);
+
+/* limits[b] = 1 + index of the last live key of batch row b (0 when none), limits[batch] = their maximum:
+ * trim_limits(kmask, 1) of packed_attn.py:123-129, concatenated as volta.py:212-213 passes them. */
+CFK_API int cfk_trim_limits(const uint8_t* kmask, int32_t* limits, int batch, int s, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CFK_B200_H_ */
