@@ -1,0 +1,238 @@
+// Triangle-multiplication contraction as a persistent tcgen05 batched GEMM:
+//   out[c, i, j] = alpha * sum_k a[c, i, k] * b[c, j, k],   a [C,I,K], b [C,J,K] (bf16 or e4m3), out [C,I,J] bf16.
+// One CTA per SM walks 128 x 256 output tiles (c outermost, so the tiles in flight share operands in L2).
+//   warp 0     TMA producer: 128-byte-wide K slices of A (128 rows) and B (256 rows) into a 4-stage ring
+//   warp 1     MMA issuer: four K=32-byte tcgen05.mma per slice into one of two 256-column TMEM accumulators
+//   warps 2-5  epilogue: TMEM -> registers -> bf16 -> swizzled shared staging -> TMA store, overlapped with the
+//              next tile's main loop through the second accumulator
+// bf16 and e4m3 differ only in the tensor-map element type and the instruction descriptor: both move 128-byte
+// rows and advance the descriptors by 32 bytes per MMA.
+// Math: src/colabfold_kernels/contract.py:1-4,56-57 (e4m3) and the XLA batched GEMM of tri_mul.py:6-7 (bf16).
+#include "attention_sm100.cuh"
+
+namespace cfk {
+namespace {
+
+constexpr int kTM = 128, kTN = 256;
+constexpr int kStages = 4;
+constexpr int kSliceA = kTM * 128, kSliceB = kTN * 128;  // bytes per stage
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kSliceA;
+constexpr int kOffStage = kOffB + kStages * kSliceB;  // epilogue staging: two [128 x 128 B] boxes
+constexpr int kStageBytes = 2 * kTM * 128;
+constexpr int kOffBar = kOffStage + kStageBytes;
+constexpr int kNumBars = 2 * kStages + 4;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kSmem = kOffTmem + 16 + 1024;
+static_assert(kSmem <= 232448, "shared memory budget");
+constexpr int kThreads = 192;
+
+struct ContractParams {
+  int C, I, J, K;       // K in ELEMENTS
+  int k_per_slice;      // elements per 128-byte slice (64 bf16, 128 e4m3)
+  int is_f8;
+  float alpha;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const __grid_constant__ CUtensorMap tm_o, const ContractParams prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  {
+    __shared__ int s_abort;
+    if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(prm.status);
+    __syncthreads();
+    if (s_abort != 0) return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int ti = (prm.I + kTM - 1) / kTM, tj = (prm.J + kTN - 1) / kTN;
+  const int ntiles = prm.C * ti * tj;
+  const int nslices = (prm.K + prm.k_per_slice - 1) / prm.k_per_slice;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_o);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int c = tile / (ti * tj), rem = tile % (ti * tj), i0 = (rem / tj) * kTM, j0 = (rem % tj) * kTN;
+        for (int s = 0; s < nslices; ++s, ++it) {
+          const int st = it % kStages;
+          ok = mbar_wait_deadline(&empty[st], ((it / kStages) & 1) ^ 1);
+          if (!ok) { report_timeout(prm.status, 401); break; }
+          mbar_arrive_expect_tx(&full[st], kSliceA + kSliceB);
+          tma_load_3d(smem + kOffA + st * kSliceA, &tm_a, &full[st], s * prm.k_per_slice, i0, c);
+          tma_load_3d(smem + kOffB + st * kSliceB, &tm_b, &full[st], s * prm.k_per_slice, j0, c);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = prm.is_f8 ? make_idesc(kTM, kTN, 0, 0, 0, 0) : make_idesc(kTM, kTN, 1, 1, 0, 0);
+      const uint32_t a_base = smem_u32(smem + kOffA), b_base = smem_u32(smem + kOffB);
+      int it = 0, n = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++n) {
+        const int acc = n & 1;
+        ok = mbar_wait_deadline(&acc_empty[acc], ((n >> 1) & 1) ^ 1);
+        if (!ok) { report_timeout(prm.status, 402); break; }
+        tc_fence_after();
+        for (int s = 0; s < nslices; ++s, ++it) {
+          const int st = it % kStages;
+          ok = mbar_wait_deadline(&full[st], (it / kStages) & 1);
+          if (!ok) { report_timeout(prm.status, 403); break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a = desc_k_major(a_base + st * kSliceA + kk * 32, 128);
+            const uint64_t b = desc_k_major(b_base + st * kSliceB + kk * 32, 128);
+            if (prm.is_f8) mma_f8_ss(tmem + acc * kTN, a, b, idesc, (s | kk) != 0);
+            else mma_f16_ss(tmem + acc * kTN, a, b, idesc, (s | kk) != 0);
+          }
+          mma_commit(&empty[st]);
+        }
+        if (ok) mma_commit(&acc_full[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3, row = quad * 32 + lane;
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    const bool issuer = warp == 2 && lane == 0;
+    uint8_t* stage = smem + kOffStage;
+    int n = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++n) {
+      const int c = tile / (ti * tj), rem = tile % (ti * tj), i0 = (rem / tj) * kTM, j0 = (rem % tj) * kTN;
+      const int acc = n & 1;
+      if (ok && !mbar_wait_deadline(&acc_full[acc], (n >> 1) & 1)) {
+        report_timeout(prm.status, 404);
+        ok = false;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        if (issuer) tma_wait_group_read<0>();  // the previous store has finished reading the staging tile
+        named_bar_sync(1, 128);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t r[32];
+          tmem_ld_x32(tmem + lane_addr + acc * kTN + half * 128 + cc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]) * prm.alpha, __uint_as_float(r[q * 8 + 1]) * prm.alpha);
+            w.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]) * prm.alpha, __uint_as_float(r[q * 8 + 3]) * prm.alpha);
+            w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]) * prm.alpha, __uint_as_float(r[q * 8 + 5]) * prm.alpha);
+            w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]) * prm.alpha, __uint_as_float(r[q * 8 + 7]) * prm.alpha);
+            const int chunk = cc * 4 + q;  // 16-byte chunk inside the 256-byte half row
+            *reinterpret_cast<uint4*>(stage + (chunk / 8) * (kTM * 128) + swz_off(row, chunk % 8, 128)) = w;
+          }
+        }
+        fence_proxy_async();
+        named_bar_sync(1, 128);
+        if (issuer && ok) {
+          tma_store_3d(&tm_o, stage, j0 + half * 128, i0, c);
+          tma_store_3d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0, c);
+          tma_commit_group();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+    if (issuer) tma_wait_group<0>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+}  // namespace cfk
+
+using namespace cfk;
+
+extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
+                            void* stream) {
+  if (a == nullptr || b == nullptr || out == nullptr) return CFK_ERR_NULL;
+  if (c <= 0 || i <= 0 || j <= 0 || k <= 0) return CFK_ERR_SHAPE;
+  if (dtype != CFK_BF16 && dtype != CFK_E4M3) return CFK_ERR_DTYPE;
+  const int es = dtype == CFK_BF16 ? 2 : 1;
+  // TMA strides are multiples of 16 bytes: K rows of the operands, J rows of the bf16 product
+  if ((int64_t(k) * es) % 16 != 0 || j % 8 != 0) return CFK_ERR_SHAPE;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(out)) return CFK_ERR_ALIGN;
+  CUtensorMap ta, tb, to;
+  {
+    uint64_t dims[3] = {uint64_t(k), uint64_t(i), uint64_t(c)};
+    uint64_t str[2] = {uint64_t(k) * es, uint64_t(i) * k * es};
+    uint32_t box[3] = {uint32_t(128 / es), kTM, 1};
+    int rc = make_tensor_map(&ta, a, dtype, 3, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  }
+  {
+    uint64_t dims[3] = {uint64_t(k), uint64_t(j), uint64_t(c)};
+    uint64_t str[2] = {uint64_t(k) * es, uint64_t(j) * k * es};
+    uint32_t box[3] = {uint32_t(128 / es), kTN, 1};
+    int rc = make_tensor_map(&tb, b, dtype, 3, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  }
+  {
+    uint64_t dims[3] = {uint64_t(j), uint64_t(i), uint64_t(c)};
+    uint64_t str[2] = {uint64_t(j) * 2, uint64_t(i) * j * 2};
+    uint32_t box[3] = {64, kTM, 1};
+    int rc = make_tensor_map(&to, out, CFK_BF16, 3, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  }
+  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word()};
+  if (prm.status == nullptr) return CFK_ERR_LAUNCH;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return CFK_ERR_LAUNCH;
+    attr_set = true;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ntiles = int64_t(c) * ((i + kTM - 1) / kTM) * ((j + kTN - 1) / kTN);
+  const int grid = int(ntiles < sms ? ntiles : sms);
+  contract_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(ta, tb, to, prm);
+  return check_launch();
+}

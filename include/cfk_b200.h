@@ -95,6 +95,15 @@ CFK_API int cfk_packed_attention_fwd(const void* p, const void* bias, const uint
  * trim_limits(kmask, 1) of packed_attn.py:123-129, concatenated as volta.py:212-213 passes them. */
 CFK_API int cfk_trim_limits(const uint8_t* kmask, int32_t* limits, int batch, int s, void* stream);
 
+/* ---- Triangle-multiplication contraction ---------------------------------------------------------------
+ * out[c,i,j] = alpha * sum_k a[c,i,k] * b[c,j,k]; a [C,I,K], b [C,J,K] in `dtype` (CFK_BF16, or CFK_E4M3 with
+ * alpha = scale_a * scale_b, 1.0 for the reference's unscaled saturating cast); out [C,I,J] bf16; fp32
+ * accumulation.  K * itemsize must be a multiple of 16 and J of 8 (the reference's own rule, contract.py:43-45).
+ * Replaces CckFp8Contract (contract.py:48-53; no workspace output is needed here) and the XLA batched GEMM the
+ * bf16 path is left to (tri_mul.py:6-7). */
+CFK_API int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif
