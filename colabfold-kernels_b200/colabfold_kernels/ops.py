@@ -133,3 +133,15 @@ def packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=False, trim
     _lib.call("cfk_packed_attention_fwd", _ptr(p), _ptr(bias), _ptr(km), _ptr(gb), _ptr(out), _ptr(lse), _ptr(lim),
               x, y, g, h, d, tag(p.dtype), int(column), float(sm_scale), _stream())
   return (out, lse) if want_lse else out
+
+
+# ------------------------------------------------------------------------------------------ contraction
+def contract(a, b, alpha=1.0):
+  """out[c,i,j] = alpha * sum_k a[c,i,k] b[c,j,k]; a, b bf16 or float8_e4m3fn -> bf16."""
+  a, b = _c(a), _c(b)
+  c, i, k = a.shape
+  j = b.shape[1]
+  out = torch.empty((c, i, j), dtype=torch.bfloat16, device=a.device)
+  with torch.cuda.device(a.device):
+    _lib.call("cfk_contract", _ptr(a), _ptr(b), _ptr(out), c, i, j, k, tag(a.dtype), float(alpha), _stream())
+  return out

@@ -1,14 +1,20 @@
 // Bias-fused flash attention forward for sm_100a: TMA-staged tiles, tcgen05 MMAs, TMEM accumulators.
 //
 // One CTA owns a 128-query tile of one head for G batch rows that share the same [128 x Sk] slice of the
-// per-head bias (the bias is read once per key block and reused for G score tiles).  Warp roles:
-//   warp 0      TMA producer: Q tiles (once), bias tile per key block, K/V tiles per (key block, batch row)
-//   warp 1      MMA issuer:   S = Q K^T into TMEM (double buffered), then O += P V (P staged in shared memory)
-//   warps 2-5   softmax group 0 (batch rows 0, 2, ...), one thread per query row = one TMEM lane
-//   warps 6-9   softmax group 1 (batch rows 1, 3, ...)
+// per-head bias (the bias is read once per key block and reused for G score tiles).  A "step" is one
+// (key block j, batch row g) pair; steps alternate between two softmax groups so that one group's
+// exponentials overlap the other's MMAs.  Warp roles (warpgroup 0 hands its registers to the others):
+//   warp 0      TMA producer: Q tiles (once), bias tile per key block, K tile per step
+//   warp 1      MMA issuer:   S = Q K^T (SS, two steps ahead), O += P V (TS: P is read from TMEM)
+//   warp 2      key-mask producer: per step 128 additive floats (0 / floor / -inf) in shared memory
+//   warp 3      TMA producer: V tile per step
+//   warps 4-7   softmax group 0 (batch rows 0, 2, ...), one thread per query row = one TMEM lane
+//   warps 8-11  softmax group 1 (batch rows 1, 3, ...)
+// TMEM columns: S0 [0,128) S1 [128,256) | P0 [256,320) P1 [320,384) (bf16 pairs) | O_g [384 + g*D, +D).
 // Softmax is online in the natural-log domain with a lazily updated reference maximum; masked keys are an
 // additive per-key floor, keys past Sk an additive -inf.  Every barrier wait is deadline-bounded and reports
-// into the status word instead of hanging.
+// into the status word instead of hanging.  The MMA-issuing thread is scalar code on one lane: it only adds
+// constants to descriptors built once, because every extra instruction there delays the tensor pipe.
 // Math: src/colabfold_kernels/tri_flash.py:132-167,215-239; gate: packed_attn.py:157-158.
 #include "attention_sm100.cuh"
 
@@ -18,31 +24,31 @@ namespace {
 
 template <int D>
 struct FwdCfg {
-  static constexpr int G = D <= 32 ? 4 : 2;        // batch rows per CTA
-  static constexpr int kStages = D <= 32 ? 3 : 2;  // K/V ring depth
+  static constexpr int G = 128 / D;  // batch rows per CTA: their O accumulators fill 128 TMEM columns
+  static constexpr int kStages = 4;  // K ring and V ring depth
   static constexpr int kRowBytes = D * 2;
   static constexpr int kTileQkv = kBQ * kRowBytes;
   static constexpr int kTileBias = kBQ * kBK * 2;  // two 64-key halves, 128-byte swizzled rows
-  static constexpr int kTileP = kBQ * kBK * 2;
+  static constexpr int kMaskSlots = 4;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + G * kTileQkv;
   static constexpr int kOffV = kOffK + kStages * kTileQkv;
   static constexpr int kOffBias = kOffV + kStages * kTileQkv;
-  static constexpr int kOffP = kOffBias + 2 * kTileBias;
-  static constexpr int kOffMask = kOffP + 2 * kTileP;          // float [2 groups][2 buffers][128]
-  static constexpr int kOffFlag = kOffMask + 2 * 2 * 128 * 4;  // int [2 groups][2 buffers][4 warps]
-  static constexpr int kOffBar = kOffFlag + 2 * 2 * 4 * 4;
-  static constexpr int kNumBars = G + 2 * kStages + 4 + 4 + 4;
+  static constexpr int kOffMask = kOffBias + 2 * kTileBias;         // float [kMaskSlots][128] additive key mask
+  static constexpr int kOffFlag = kOffMask + kMaskSlots * 128 * 4;  // int [kMaskSlots]: any key masked / past Sk
+  static constexpr int kOffState = kOffFlag + 16;                   // float [2][G][128]: reference max, row sum
+  static constexpr int kOffBar = kOffState + 2 * G * 128 * 4;
+  static constexpr int kNumBars = G + 4 * kStages + 4 + 4 + 4 + 2 * kMaskSlots;
   static constexpr int kOffTmem = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffTmem + 16;
   static constexpr int kTmemCols = 512;
-  static constexpr int kColS = 0;    // S buffers at columns 0 and 128
-  static constexpr int kColO = 256;  // O_g at 256 + g * D
-  static_assert(256 + G * D <= 512, "TMEM budget");
+  static constexpr int kColS = 0, kColP = 256, kColO = 384;
+  static_assert(kColO + G * D <= 512, "TMEM budget");
   static_assert(kSmemBytes + 1024 <= 232448, "shared memory budget");
+  static_assert(kMaskSlots * 4 <= 16, "flag area");
 };
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 
 struct FwdParams {
   AttnProblem p;
@@ -57,6 +63,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                       const FwdParams prm) {
   using C = FwdCfg<D>;
   constexpr int G = C::G;
+  constexpr int ST = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: swizzled tiles and UMMA descriptors assume it
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -70,15 +77,19 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  uint64_t* q_full = bars;                      // [G]
-  uint64_t* kv_full = q_full + G;               // [kStages]
-  uint64_t* kv_empty = kv_full + C::kStages;    // [kStages]
-  uint64_t* bias_full = kv_empty + C::kStages;  // [2]
-  uint64_t* bias_empty = bias_full + 2;         // [2]
-  uint64_t* s_full = bias_empty + 2;            // [2]
-  uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;               // [2]
-  uint64_t* pv_done = p_full + 2;               // [2]
+  uint64_t* q_full = bars;                 // [G]
+  uint64_t* k_full = q_full + G;           // [ST]
+  uint64_t* k_empty = k_full + ST;         // [ST]
+  uint64_t* v_full = k_empty + ST;         // [ST]
+  uint64_t* v_empty = v_full + ST;         // [ST]
+  uint64_t* bias_full = v_empty + ST;      // [2]
+  uint64_t* bias_empty = bias_full + 2;    // [2]
+  uint64_t* s_full = bias_empty + 2;       // [2]
+  uint64_t* s_empty = s_full + 2;          // [2]
+  uint64_t* p_full = s_empty + 2;          // [2]
+  uint64_t* pv_done = p_full + 2;          // [2]
+  uint64_t* mask_full = pv_done + 2;       // [kMaskSlots]
+  uint64_t* mask_empty = mask_full + C::kMaskSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -92,9 +103,11 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < G; ++i) mbar_init(&q_full[i], 1);
-    for (int i = 0; i < C::kStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bias_full[i], 1);
@@ -103,6 +116,10 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
+    }
+    for (int i = 0; i < C::kMaskSlots; ++i) {
+      mbar_init(&mask_full[i], 1);
+      mbar_init(&mask_empty[i], 4);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -119,102 +136,151 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      bool ok = true;
-      for (int g = 0; g < gcount; ++g) {
-        mbar_arrive_expect_tx(&q_full[g], C::kTileQkv);
-        tma_load_4d(smem + C::kOffQ + g * C::kTileQkv, &tm_q, &q_full[g], 0, q0, head, b0 + g);
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
+    if (warp == 0) {
+      // ---------------------------------------------------------------- TMA producer: Q, bias, K
+      if (lane == 0) {
+        bool ok = true;
+        for (int g = 0; g < gcount; ++g) {
+          mbar_arrive_expect_tx(&q_full[g], C::kTileQkv);
+          tma_load_4d(smem + C::kOffQ + g * C::kTileQkv, &tm_q, &q_full[g], 0, q0, head, b0 + g);
+        }
+        int step = 0;
+        for (int j = 0; j < nj && ok; ++j) {
+          if (prm.has_bias) {
+            const int bb = j & 1;
+            ok = mbar_wait_deadline(&bias_empty[bb], ((j >> 1) & 1) ^ 1);
+            if (!ok) { report_timeout(prm.status, 101); break; }
+            mbar_arrive_expect_tx(&bias_full[bb], C::kTileBias);
+            uint8_t* dst = smem + C::kOffBias + bb * C::kTileBias;
+            tma_load_3d(dst, &tm_bias, &bias_full[bb], j * kBK, q0, head);
+            tma_load_3d(dst + C::kTileBias / 2, &tm_bias, &bias_full[bb], j * kBK + 64, q0, head);
+          }
+          for (int g = 0; g < gcount; ++g, ++step) {
+            const int st = step % ST;
+            ok = mbar_wait_deadline(&k_empty[st], ((step / ST) & 1) ^ 1);
+            if (!ok) { report_timeout(prm.status, 102); break; }
+            mbar_arrive_expect_tx(&k_full[st], C::kTileQkv);
+            tma_load_4d(smem + C::kOffK + st * C::kTileQkv, &tm_k, &k_full[st], 0, j * kBK, head, b0 + g);
+          }
+        }
       }
-      int step = 0;
-      for (int j = 0; j < nj && ok; ++j) {
-        if (prm.has_bias) {
-          const int bb = j & 1;
-          ok = mbar_wait_deadline(&bias_empty[bb], ((j >> 1) & 1) ^ 1);
-          if (!ok) { report_timeout(prm.status, 101); break; }
-          mbar_arrive_expect_tx(&bias_full[bb], C::kTileBias);
-          uint8_t* dst = smem + C::kOffBias + bb * C::kTileBias;
-          tma_load_3d(dst, &tm_bias, &bias_full[bb], j * kBK, q0, head);
-          tma_load_3d(dst + C::kTileBias / 2, &tm_bias, &bias_full[bb], j * kBK + 64, q0, head);
-        }
-        for (int g = 0; g < gcount; ++g, ++step) {
-          const int st = step % C::kStages;
-          ok = mbar_wait_deadline(&kv_empty[st], ((step / C::kStages) & 1) ^ 1);
-          if (!ok) { report_timeout(prm.status, 102); break; }
-          mbar_arrive_expect_tx(&kv_full[st], 2 * C::kTileQkv);
-          tma_load_4d(smem + C::kOffK + st * C::kTileQkv, &tm_k, &kv_full[st], 0, j * kBK, head, b0 + g);
-          tma_load_4d(smem + C::kOffV + st * C::kTileQkv, &tm_v, &kv_full[st], 0, j * kBK, head, b0 + g);
+      __syncwarp();
+    } else if (warp == 3) {
+      // ---------------------------------------------------------------- TMA producer: V
+      if (lane == 0) {
+        for (int step = 0; step < nsteps; ++step) {
+          const int st = step % ST, g = step % gcount, j = step / gcount;
+          if (!mbar_wait_deadline(&v_empty[st], ((step / ST) & 1) ^ 1)) { report_timeout(prm.status, 103); break; }
+          mbar_arrive_expect_tx(&v_full[st], C::kTileQkv);
+          tma_load_4d(smem + C::kOffV + st * C::kTileQkv, &tm_v, &v_full[st], 0, j * kBK, head, b0 + g);
         }
       }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc(kBQ, kBK, 1, 1, 0, 0);
-      constexpr uint32_t idesc_pv = make_idesc(kBQ, D, 1, 1, 0, 1);
-      const uint32_t q_base = smem_u32(smem + C::kOffQ), k_base = smem_u32(smem + C::kOffK);
-      const uint32_t v_base = smem_u32(smem + C::kOffV), p_base = smem_u32(smem + C::kOffP);
-      uint32_t s_uses[2] = {0, 0}, p_uses[2] = {0, 0};
+      __syncwarp();
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = make_idesc(kBQ, kBK, 1, 1, 0, 0);
+        constexpr uint32_t idesc_pv = make_idesc(kBQ, D, 1, 1, 0, 1);
+        constexpr uint32_t kTile16 = C::kTileQkv >> 4;
+        const uint64_t q_desc0 = desc_k_major(smem_u32(smem + C::kOffQ), C::kRowBytes);
+        const uint64_t k_desc0 = desc_k_major(smem_u32(smem + C::kOffK), C::kRowBytes);
+        const uint64_t v_desc0 = desc_mn_major(smem_u32(smem + C::kOffV), C::kRowBytes, 0);
+        // Scalar state advanced by increments only: one lane runs this, and every division or re-derivation
+        // here would sit between two MMAs.
+        int s_g = 0, s_st = 0, p_g = 0, p_st = 0;
+        uint32_t k_par = 0, v_par = 0, s_first = 1, p_first = 1;
+        uint32_t se_par0 = 1, se_par1 = 1, pf_par0 = 0, pf_par1 = 0;
+        bool ok = true;
+        auto issue_s = [&]() {
+          const int buf = s_g & 1;
+          if (s_first && !mbar_wait_deadline(&q_full[s_g], 0)) { report_timeout(prm.status, 201); return false; }
+          if (!mbar_wait_deadline(&k_full[s_st], k_par)) { report_timeout(prm.status, 202); return false; }
+          if (!mbar_wait_deadline(&s_empty[buf], buf ? se_par1 : se_par0)) { report_timeout(prm.status, 203); return false; }
+          tc_fence_after();
+          const uint64_t a = q_desc0 + uint64_t(s_g * kTile16), b = k_desc0 + uint64_t(s_st * kTile16);
+          const uint32_t d = tmem + C::kColS + buf * kBK;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
+          mma_commit(&k_empty[s_st]);
+          mma_commit(&s_full[buf]);
+          if (buf) se_par1 ^= 1; else se_par0 ^= 1;
+          if (++s_g == gcount) { s_g = 0; s_first = 0; }
+          if (++s_st == ST) { s_st = 0; k_par ^= 1; }
+          return true;
+        };
+        auto issue_pv = [&]() {
+          const int buf = p_g & 1;
+          if (!mbar_wait_deadline(&v_full[p_st], v_par)) { report_timeout(prm.status, 204); return false; }
+          if (!mbar_wait_deadline(&p_full[buf], buf ? pf_par1 : pf_par0)) { report_timeout(prm.status, 205); return false; }
+          tc_fence_after();
+          const uint64_t b = v_desc0 + uint64_t(p_st * kTile16);
+          const uint32_t d = tmem + C::kColO + p_g * D, a = tmem + C::kColP + buf * (kBK / 2);
+          const uint32_t acc0 = p_first ^ 1;  // key block 0 overwrites the accumulator
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16_ts(d, a + kk * 8, b + uint64_t(kk * ((16 * C::kRowBytes) >> 4)), idesc_pv, kk > 0 ? 1u : acc0);
+          mma_commit(&v_empty[p_st]);
+          mma_commit(&pv_done[buf]);
+          if (buf) pf_par1 ^= 1; else pf_par0 ^= 1;
+          if (++p_g == gcount) { p_g = 0; p_first = 0; }
+          if (++p_st == ST) { p_st = 0; v_par ^= 1; }
+          return true;
+        };
+        ok = issue_s();
+        if (ok && nsteps > 1) ok = issue_s();
+        for (int t = 0; t < nsteps && ok; ++t) {
+          ok = issue_pv();
+          if (ok && t + 2 < nsteps) ok = issue_s();
+        }
+      }
+      __syncwarp();
+    } else {
+      // ---------------------------------------------------------------- key-mask producer
+      // Per step: 128 additive floats (0 live, floor masked, -inf past Sk) and an "any" flag, a few steps ahead
+      // of the softmax groups so the global-memory latency is off their critical path.
+      float* mask_ring = reinterpret_cast<float*>(smem + C::kOffMask);
+      int* flag_ring = reinterpret_cast<int*>(smem + C::kOffFlag);
       bool ok = true;
-      auto issue_s = [&](int t) {
-        const int g = t % gcount, buf = g & 1, st = t % C::kStages;
-        if (!mbar_wait_deadline(&q_full[g], 0)) { report_timeout(prm.status, 201); return false; }
-        if (!mbar_wait_deadline(&kv_full[st], (t / C::kStages) & 1)) { report_timeout(prm.status, 202); return false; }
-        if (!mbar_wait_deadline(&s_empty[buf], (s_uses[buf] & 1) ^ 1)) { report_timeout(prm.status, 203); return false; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = desc_k_major(q_base + g * C::kTileQkv + kk * 32, C::kRowBytes);
-          const uint64_t b = desc_k_major(k_base + st * C::kTileQkv + kk * 32, C::kRowBytes);
-          mma_f16_ss(tmem + C::kColS + buf * kBK, a, b, idesc_s, kk > 0);
-        }
-        mma_commit(&s_full[buf]);
-        ++s_uses[buf];
-        return true;
-      };
-      auto issue_pv = [&](int t) {
-        const int g = t % gcount, j = t / gcount, buf = g & 1, st = t % C::kStages;
-        if (!mbar_wait_deadline(&p_full[buf], p_uses[buf] & 1)) { report_timeout(prm.status, 204); return false; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t a =
-              desc_k_major(p_base + buf * C::kTileP + (kk / 4) * (C::kTileP / 2) + (kk % 4) * 32, 128);
-          const uint64_t b = desc_mn_major(v_base + st * C::kTileQkv + kk * 16 * C::kRowBytes, C::kRowBytes, 0);
-          mma_f16_ss(tmem + C::kColO + g * D, a, b, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&kv_empty[st]);
-        mma_commit(&pv_done[buf]);
-        ++p_uses[buf];
-        return true;
-      };
-      ok = issue_s(0);
       for (int t = 0; t < nsteps && ok; ++t) {
-        if (t + 1 < nsteps) ok = issue_s(t + 1);
-        if (ok) ok = issue_pv(t);
+        const int g = t % gcount, j = t / gcount, slot = t % C::kMaskSlots;
+        if (lane == 0) ok = mbar_wait_deadline(&mask_empty[slot], ((t / C::kMaskSlots) & 1) ^ 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) { if (lane == 0) report_timeout(prm.status, 501); break; }
+        const int key = j * kBK + lane * 4;
+        float4 add = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (key < p.sk) {  // Sk is a multiple of 8, so a group of four keys is in or out as a whole
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(p.kmask + int64_t(b0 + g) * p.sk + key);
+          add.x = (w & 0x000000ffu) ? 0.f : kFloorNat;
+          add.y = (w & 0x0000ff00u) ? 0.f : kFloorNat;
+          add.z = (w & 0x00ff0000u) ? 0.f : kFloorNat;
+          add.w = (w & 0xff000000u) ? 0.f : kFloorNat;
+        }
+        *reinterpret_cast<float4*>(mask_ring + slot * 128 + lane * 4) = add;
+        const unsigned any = __ballot_sync(0xffffffffu, add.x != 0.f || add.y != 0.f || add.z != 0.f || add.w != 0.f);
+        if (lane == 0) flag_ring[slot] = any != 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&mask_full[slot]);
       }
     }
-    __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax groups
-    const int grp = (warp - 2) >> 2;           // 0 or 1
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    const int grp = (warp - 4) >> 2;           // 0 or 1
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may touch
     const int row = quad * 32 + lane;          // query row inside the tile = TMEM lane
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    const int gtid = quad * 32 + lane;         // 0..127 inside the group (distinct per thread)
-    float* mask_buf = reinterpret_cast<float*>(smem + C::kOffMask) + grp * 2 * 128;
-    int* flag_buf = reinterpret_cast<int*>(smem + C::kOffFlag) + grp * 2 * 4;
-    constexpr int kMine = (G + 1) / 2;
-    float m_ref[kMine], l_sum[kMine];
-#pragma unroll
-    for (int i = 0; i < kMine; ++i) { m_ref[i] = 0.f; l_sum[i] = 0.f; }
+    const float* mask_ring = reinterpret_cast<const float*>(smem + C::kOffMask);
+    const int* flag_ring = reinterpret_cast<const int*>(smem + C::kOffFlag);
+    // running (reference maximum, row sum) of each batch row this thread serves: [g][row], private to the thread
+    float* st_m = reinterpret_cast<float*>(smem + C::kOffState) + row;
+    float* st_l = st_m + G * 128;
     uint32_t uses = 0;  // steps this group has processed: parity of s_full / pv_done for its buffer
     bool ok = true;
     const float scale = p.scale;
     // A wait that runs out clears `ok`; later waits are then skipped but every thread still walks the
-    // same loop (named barriers stay matched) and nothing is stored.
+    // same loop and nothing is stored.
 #define CFK_SOFTMAX_WAIT(bar, parity, code)                       \
   if (ok && !mbar_wait_deadline((bar), (parity))) {               \
     report_timeout(prm.status, (code));                           \
@@ -222,27 +288,11 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   }
     const int jmax = grp < ngroups ? nj : 0;
     for (int j = 0; j < jmax; ++j) {
-      const int k0 = j * kBK;
       const uint8_t* bias_tile = smem + C::kOffBias + (j & 1) * C::kTileBias;
       if (prm.has_bias) CFK_SOFTMAX_WAIT(&bias_full[j & 1], (j >> 1) & 1, 301)
-#pragma unroll
-      for (int gi = 0; gi < kMine; ++gi) {
-        const int g = grp + 2 * gi;
-        if (g >= gcount) break;
-        const int b = b0 + g;
-        // additive key mask for this (batch row, key block): 0 live, floor masked, -inf past Sk
-        const int mb = uses & 1;
-        {
-          const int key = k0 + gtid;
-          float add = 0.f;
-          if (key >= p.sk) add = -INFINITY;
-          else if (p.kmask[int64_t(b) * p.sk + key] == 0) add = kFloorNat;
-          mask_buf[mb * 128 + gtid] = add;
-          const unsigned any = __ballot_sync(0xffffffffu, add != 0.f);
-          if (lane == 0) flag_buf[mb * 4 + quad] = any != 0;
-        }
-        named_bar_sync(1 + grp, 128);
-        const bool any_mask = (flag_buf[mb * 4 + 0] | flag_buf[mb * 4 + 1] | flag_buf[mb * 4 + 2] | flag_buf[mb * 4 + 3]) != 0;
+#pragma unroll 1
+      for (int g = grp; g < gcount; g += 2) {
+        const int t = j * gcount + g, slot = t % C::kMaskSlots;
 
         CFK_SOFTMAX_WAIT(&s_full[grp], uses & 1, 302)
         tc_fence_after();
@@ -256,7 +306,6 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         if (lane == 0) mbar_arrive(&s_empty[grp]);
 
         // logits t = scale * s + bias (+ mask), row maximum
-        float mx = -INFINITY;
         if (prm.has_bias) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
@@ -272,37 +321,54 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #pragma unroll
           for (int i = 0; i < kBK; ++i) s[i] *= scale;
         }
-        if (any_mask) {
+        CFK_SOFTMAX_WAIT(&mask_full[slot], (t / C::kMaskSlots) & 1, 305)
+        if (flag_ring[slot] != 0) {
 #pragma unroll
           for (int c = 0; c < kBK / 4; ++c) {
-            const float4 a = *reinterpret_cast<const float4*>(mask_buf + mb * 128 + c * 4);
+            const float4 a = *reinterpret_cast<const float4*>(mask_ring + slot * 128 + c * 4);
             s[c * 4 + 0] += a.x; s[c * 4 + 1] += a.y; s[c * 4 + 2] += a.z; s[c * 4 + 3] += a.w;
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&mask_empty[slot]);
+        float mx;
+        {
+          // four independent chains: two warps per scheduler cannot hide a 128-long dependent chain
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kBK; ++i) mx = fmaxf(mx, s[i]);
+          for (int i = 0; i < kBK; i += 4) {
+            m0 = fmaxf(m0, s[i]); m1 = fmaxf(m1, s[i + 1]); m2 = fmaxf(m2, s[i + 2]); m3 = fmaxf(m3, s[i + 3]);
+          }
+          mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        }
 
         // lazily updated reference maximum
-        float corr = 1.0f;
+        float corr = 1.0f, m_ref = mx, l_run = 0.f;
         bool need = false;
-        if (j == 0) {
-          m_ref[gi] = mx;
-        } else if (mx > m_ref[gi] + kRescaleSlack) {
-          corr = ex2_approx(fmaf(m_ref[gi], kLog2eF, -mx * kLog2eF));
-          m_ref[gi] = mx;
-          need = true;
+        if (j > 0) {
+          m_ref = st_m[g * 128];
+          l_run = st_l[g * 128];
+          if (mx > m_ref + kRescaleSlack) {
+            corr = ex2_approx(fmaf(m_ref, kLog2eF, -mx * kLog2eF));
+            m_ref = mx;
+            need = true;
+          }
         }
-        const float neg_m = -m_ref[gi] * kLog2eF;
-        float sum = 0.f;
+        const float neg_m = -m_ref * kLog2eF;
+        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
         uint32_t pk[kBK / 2];
 #pragma unroll
-        for (int i = 0; i < kBK / 2; ++i) {
+        for (int i = 0; i < kBK / 2; i += 2) {
           const float e0 = ex2_approx(fmaf(s[2 * i], kLog2eF, neg_m));
           const float e1 = ex2_approx(fmaf(s[2 * i + 1], kLog2eF, neg_m));
-          sum += e0 + e1;
+          const float e2 = ex2_approx(fmaf(s[2 * i + 2], kLog2eF, neg_m));
+          const float e3 = ex2_approx(fmaf(s[2 * i + 3], kLog2eF, neg_m));
+          sum0 += e0; sum1 += e1; sum2 += e2; sum3 += e3;
           pk[i] = pack_bf16x2(e0, e1);
+          pk[i + 1] = pack_bf16x2(e2, e3);
         }
-        l_sum[gi] = l_sum[gi] * corr + sum;
+        st_m[g * 128] = m_ref;
+        st_l[g * 128] = l_run * corr + ((sum0 + sum1) + (sum2 + sum3));
 
         // the previous P V of this buffer must be complete before P is overwritten or O is rescaled
         if (uses > 0) {
@@ -319,15 +385,12 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
             tmem_st_x16(tmem + lane_addr + C::kColO + g * D + c * 16, r);
           }
-          tmem_wait_st();
         }
-        uint8_t* p_tile = smem + C::kOffP + grp * C::kTileP;
+        // P (bf16 pairs) into this group's TMEM operand buffer: column c holds keys 2c, 2c+1
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 w = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
-          *reinterpret_cast<uint4*>(p_tile + (c / 8) * (C::kTileP / 2) + swz_off(row, c % 8, 128)) = w;
-        }
-        fence_proxy_async();
+        for (int c = 0; c < kBK / 32; ++c)
+          tmem_st_x16(tmem + lane_addr + C::kColP + grp * (kBK / 2) + c * 16, reinterpret_cast<uint32_t(&)[16]>(pk[c * 16]));
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[grp]);
@@ -346,24 +409,18 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #undef CFK_SOFTMAX_WAIT
     if (ok) {
       const int q = q0 + row;
-#pragma unroll
-      for (int gi = 0; gi < kMine; ++gi) {
-        const int g = grp + 2 * gi;
-        if (g >= gcount) break;
+#pragma unroll 1
+      for (int g = grp; g < gcount; g += 2) {
         const int b = b0 + g;
+        const float m_ref = st_m[g * 128], l_run = st_l[g * 128];
         float o[D];
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld_x16(tmem + lane_addr + C::kColO + g * D + c * 16, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[c * 16 + i] = __uint_as_float(r[i]);
-        }
+        for (int c = 0; c < D / 16; ++c) tmem_ld_x16(tmem + lane_addr + C::kColO + g * D + c * 16, reinterpret_cast<uint32_t(&)[16]>(o[c * 16]));
+        tmem_wait_ld();
         if (q < p.sq) {
           bool zero_row = false;
           if (p.trim != nullptr) zero_row = p.trim[b] == 0 || q >= p.trim[p.nb];
-          const float inv = zero_row ? 0.f : 1.0f / l_sum[gi];
+          const float inv = zero_row ? 0.f : 1.0f / l_run;
           const __nv_bfloat16* gate =
               p.gate == nullptr ? nullptr
                                 : static_cast<const __nv_bfloat16*>(p.gate) + b * p.sg_.b + head * p.sg_.h + int64_t(q) * p.sg_.s;
@@ -389,11 +446,8 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                                  pack_bf16x2(v[6], v[7]));
             *reinterpret_cast<uint4*>(out + c * 8) = w;
           }
-          if (p.lse != nullptr) {
-            const float m = m_ref[gi];
-            p.lse[(int64_t(b) * p.h + head) * p.sq + q] =
-                m < -1e30f ? kNegRef : fmaf(m, kLog2eF, __log2f(l_sum[gi]));
-          }
+          if (p.lse != nullptr)
+            p.lse[(int64_t(b) * p.h + head) * p.sq + q] = m_ref < -1e30f ? kNegRef : fmaf(m_ref, kLog2eF, __log2f(l_run));
         }
       }
     }
@@ -425,13 +479,9 @@ int launch(const AttnProblem& p, cudaStream_t st) {
   }
   FwdParams prm{p, device_status_word(), p.bias != nullptr};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
-  static bool attr_set = false;
   const int smem = C::kSmemBytes + 1024;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(attn_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return CFK_ERR_LAUNCH;
-    attr_set = true;
-  }
+  if (cudaFuncSetAttribute(attn_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return CFK_ERR_LAUNCH;
   dim3 grid((p.nb + C::G - 1) / C::G, (p.sq + kBQ - 1) / kBQ, p.h);
   attn_fwd_sm100_kernel<D><<<grid, kThreads, smem, st>>>(tq, tk, tv, tb, prm);
   return check_launch();
@@ -446,6 +496,7 @@ bool attention_sm100_supported(const AttnProblem& p, int dtype) {
   auto ok16 = [](const void* ptr) { return ptr == nullptr || aligned16(ptr); };
   if (!ok16(p.q) || !ok16(p.k) || !ok16(p.v) || !ok16(p.bias) || !ok16(p.out) || !ok16(p.gate) || !ok16(p.gate_bias))
     return false;
+  if (reinterpret_cast<uintptr_t>(p.kmask) % 4 != 0) return false;
   auto st8 = [](const Strides& s) { return s.b % 8 == 0 && s.s % 8 == 0 && s.h % 8 == 0; };
   return st8(p.sq_) && st8(p.sk_) && st8(p.sv_) && st8(p.so_) && (p.gate == nullptr || st8(p.sg_));
 }
