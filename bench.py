@@ -1,0 +1,258 @@
+#!/usr/bin/env python
+"""Headline benchmark: bias-fused attention forward + backward at N_res = 1024 (bf16).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One "step" is one forward (with lse) plus one backward (dq, dk, dv, dbias) of MSA-row attention with pair
+bias at (batch, heads, seq, head_dim) = (512, 8, 1024, 32), 'seq' layout, Bernoulli(0.95) key mask, on
+synthetic seeded inputs.  With N > 1 (launched by torch.distributed.run, one rank per GPU) every rank runs
+its own 512 batch rows: the batch axis is independent, so there is no data-path collective ("weak" scaling).
+
+The JSON line carries:
+  value         whole-job TFLOP/s, inputs resident in HBM, CUDA-event timed, max over ranks
+  e2e           the same metric through the public selector API with pinned HOST buffers: host->device copies
+                of q, k, v, bias, mask and the cotangent and device->host copies of out, dq, dk, dv, dbias are
+                inside the timed region
+  roofline      the dominant kernel (the backward) against the measured dense-bf16 peak
+  cpu_baseline  the CPU oracle (a port of the reference's fp32 ref_attn and flash backward) timed on this
+                box's host cores on a bounded sample of the same workload
+`--impl reference` prints the CPU arm alone (the reference's own path needs JAX, which is not installed: the
+port of its jnp reference stands in, kind "port").
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "colabfold-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+B, H, S, D = 512, 8, 1024, 32
+METRIC = "biased_attention_fwd_bwd_tflops"
+WORKLOAD = f"msa_row_attention_pair_bias fwd+bwd b={B} h={H} s={S} d={D} layout=seq mask=bernoulli0.95"
+
+
+def flops(b):
+  return 14.0 * b * H * S * S * D  # 4 forward + 10 backward (five GEMMs incl. the recompute), dense
+
+
+def peaks():
+  path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+  if os.path.exists(path):
+    d = json.load(open(path))
+    return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+  return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler(threading.Thread):
+  """nvidia-smi clocks and throttle reasons every 200 ms while the timed region runs."""
+
+  def __init__(self, index):
+    super().__init__(daemon=True)
+    self.rows, self.stop_flag, self.index = [], threading.Event(), index
+
+  def run(self):
+    q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    while not self.stop_flag.is_set():
+      try:
+        out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout.strip()
+        if out:
+          self.rows.append([c.strip() for c in out.split(",")])
+      except Exception:
+        pass
+      self.stop_flag.wait(0.2)
+
+  def summary(self):
+    if not self.rows:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    mhz = sorted(int(r[0]) for r in self.rows if r[0].isdigit())
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = [n for i, n in enumerate(names) if any(r[2 + i].lower().startswith("active") for r in self.rows)]
+    mx = [int(r[1]) for r in self.rows if r[1].isdigit()]
+    return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons}
+
+
+def cpu_arm(steps, warmup, sample_b=2):
+  """The CPU oracle on a bounded sample (sample_b batch rows of the same heads/seq/head_dim), all host threads."""
+  import torch
+  import oracle as O
+  g = torch.Generator().manual_seed(0)
+  q, k, v, do = (torch.randn(sample_b, H, S, D, generator=g) for _ in range(4))
+  bias = torch.randn(H, S, S, generator=g)
+  kmask = torch.rand(sample_b, S, generator=g) < 0.95
+  scale = D ** -0.5
+
+  def step():
+    out = O.ref_attn(q, k, v, bias, kmask, scale)
+    lse = O.ref_attn_lse(q, k, bias, kmask, scale)
+    return O.ref_attn_bwd(q, k, v, bias, kmask, out, do, lse, scale)
+
+  for _ in range(max(1, min(warmup, 1))):
+    step()
+  times = []
+  for _ in range(max(1, min(steps, 3))):
+    t0 = time.perf_counter()
+    step()
+    times.append(time.perf_counter() - t0)
+  sec = sorted(times)[len(times) // 2]
+  return {"value": flops(sample_b) / sec / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+          "sample": f"{sample_b} of {B} batch rows (h={H}, s={S}, d={D}), fp32 PyTorch-CPU port of ref_attn + flash backward, "
+                    f"median of {len(times)}", "ms_per_sample": sec * 1e3}
+
+
+def main():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=5)
+  ap.add_argument("--warmup", type=int, default=3)
+  ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+  args = ap.parse_args()
+  rank = int(os.environ.get("RANK", "0"))
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+  if args.impl == "reference":
+    if rank != 0:
+      return
+    cb = cpu_arm(args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_sample"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "note": "reference's jnp path needs JAX (absent): CPU port of it, bounded sample"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return
+
+  import torch
+  import torch.distributed as dist
+  from colabfold_kernels import _lib, attention, dispatch, ops
+  if not torch.cuda.is_available():
+    raise SystemExit("bench.py needs a CUDA device: the library has no CPU path")
+  torch.cuda.set_device(local_rank)
+  dev = torch.device("cuda", local_rank)
+  if world > 1:
+    dist.init_process_group("nccl", device_id=dev)
+  lib = _lib.load()
+  bf = torch.bfloat16
+  g = torch.Generator().manual_seed(1000 + rank)
+  host = {n: torch.randn(B, S, H, D, generator=g).to(bf).pin_memory() for n in ("q", "k", "v", "do")}
+  host["bias"] = torch.randn(H, S, S, generator=g).to(bf).pin_memory()
+  mask_bool = torch.rand(B, S, generator=g) < 0.95
+  host["mask_bias"] = ((~mask_bool).to(torch.float32) * -1e9).to(bf).reshape(B, 1, 1, S).pin_memory()
+  scale = D ** -0.5
+  q, k, v, do, bias = (host[n].to(dev) for n in ("q", "k", "v", "do", "bias"))
+  kmask = mask_bool.to(dev)
+
+  def barrier():
+    if world > 1:
+      dist.barrier()
+    torch.cuda.synchronize()
+
+  fwd_ms, bwd_ms = [], []
+
+  def step(timed=False):
+    if timed:
+      e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+      e[0].record()
+    out, lse = ops.attention_fwd(q, k, v, bias, kmask, scale, seq_major=True, want_lse=True)
+    if timed:
+      e[1].record()
+    grads = ops.attention_bwd(q, k, v, bias, kmask, out, do, lse, scale, seq_major=True, want_dbias=True)
+    if timed:
+      e[2].record()
+      return e
+    return grads
+
+  for _ in range(max(args.warmup, 3)):
+    step()
+  barrier()
+  sampler = ClockSampler(local_rank)
+  if rank == 0:
+    sampler.start()
+  lib.cfk_launch_count(1)
+  t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  t0.record()
+  evs = [step(timed=True) for _ in range(args.steps)]
+  t1.record()
+  barrier()
+  launches = lib.cfk_launch_count(0)
+  ms = torch.tensor([t0.elapsed_time(t1)], device=dev)
+  if world > 1:
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+  ms_per_step = float(ms) / args.steps
+  for e in evs:
+    fwd_ms.append(e[0].elapsed_time(e[1]))
+    bwd_ms.append(e[1].elapsed_time(e[2]))
+  status = ops.device_status()
+
+  # ---- end to end through the public selector API with host buffers ---------------------------------------
+  kernel = attention(dispatch(), bf, D, D, layout="seq")
+  out_host = {n: torch.empty(B, S, H, D, dtype=bf).pin_memory() for n in ("out", "dq", "dk", "dv")}
+  out_host["dbias"] = torch.empty(H, S, S, dtype=bf).pin_memory()
+
+  def e2e_step():
+    dq_, dk_, dv_, do_ = (host[n].to(dev, non_blocking=True) for n in ("q", "k", "v", "do"))
+    db_ = host["bias"].to(dev, non_blocking=True)
+    mb_ = host["mask_bias"].to(dev, non_blocking=True)
+    for t in (dq_, dk_, dv_, db_):
+      t.requires_grad_(True)
+    o = kernel(dq_, dk_, dv_, mb_, db_, scale)
+    o.backward(do_)
+    out_host["out"].copy_(o.detach(), non_blocking=True)
+    for n, t in (("dq", dq_), ("dk", dk_), ("dv", dv_), ("dbias", db_)):
+      out_host[n].copy_(t.grad, non_blocking=True)
+
+  h2d = sum(host[n].numel() * host[n].element_size() for n in ("q", "k", "v", "do", "bias", "mask_bias"))
+  d2h = sum(t.numel() * t.element_size() for t in out_host.values())
+  e2e_step()
+  barrier()
+  n_e2e = max(1, min(args.steps, 3))
+  t0.record()
+  for _ in range(n_e2e):
+    e2e_step()
+  t1.record()
+  barrier()
+  e2e_ms = torch.tensor([t0.elapsed_time(t1) / n_e2e], device=dev)
+  if world > 1:
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+  if rank == 0:
+    sampler.stop_flag.set()
+    sampler.join(timeout=2)
+
+  if rank == 0:
+    peak_tf, _, peak_kind = peaks()
+    fwd = sorted(fwd_ms)[len(fwd_ms) // 2]
+    bwd = sorted(bwd_ms)[len(bwd_ms) // 2]
+    dominant, dom_ms, dom_flops = ("attention_bwd", bwd, 10.0 * B * H * S * S * D) if bwd >= fwd else \
+                                  ("attention_fwd", fwd, 4.0 * B * H * S * S * D)
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": flops(B) * world / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "parallelism": f"batch-sharded x{world}, no collective",
+                   "l2": "inputs (1.1 GB per rank) exceed the 126 MB L2; no flush between steps",
+                   "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
+                   "device_status": status},
+        "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "traffic": None, "peak_source": f"{peak_kind} burst bf16"},
+        "clocks": sampler.summary(),
+    }
+    line["cpu_baseline"] = {k: v for k, v in cpu_arm(3, 1).items() if k != "ms_per_sample"}
+    print(json.dumps(line))
+  if world > 1:
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+  main()

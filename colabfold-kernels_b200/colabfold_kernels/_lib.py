@@ -18,7 +18,7 @@ F32, BF16, E4M3 = 0, 1, 2
 
 _CTYPES = {
     "int": ctypes.c_int, "float": ctypes.c_float, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t,
-    "int32_t": ctypes.c_int32, "uint8_t": ctypes.c_uint8, "void": None,
+    "int32_t": ctypes.c_int32, "long long": ctypes.c_longlong, "uint8_t": ctypes.c_uint8, "void": None,
 }
 
 
@@ -40,7 +40,7 @@ def _parse_header(path):
         argt.append(ctypes.c_char_p if a.startswith("const char") else ctypes.c_void_p)
       else:
         argt.append(_CTYPES[a.replace("const ", "").split()[0]])
-    ret = ret.strip()
+    ret = " ".join(ret.split())
     rt = ctypes.c_char_p if ret == "const char*" else _CTYPES[ret]
     protos[name] = (rt, argt)
   return protos, status

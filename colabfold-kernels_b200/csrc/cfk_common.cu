@@ -2,6 +2,7 @@
 #include "cfk_common.cuh"
 
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <mutex>
 
 namespace cfk {
@@ -48,10 +49,13 @@ int make_tensor_map(CUtensorMap* map, const void* base, int dtype, int rank, con
 }
 
 namespace {
+std::atomic<long long> g_launches{0};
 constexpr int kMaxDevices = 64;
 int* g_status[kMaxDevices] = {};
 std::mutex g_status_mutex;
 }  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 // One int32 per device, allocated on first use on that device and kept for the life of the process.
 int* device_status_word() {
@@ -76,6 +80,10 @@ extern "C" int cfk_last_device_status(int reset) {
   if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return CFK_ERR_LAUNCH;
   if (reset && v != 0) cudaMemset(p, 0, sizeof(int));
   return v;
+}
+
+extern "C" long long cfk_launch_count(int reset) {
+  return reset ? cfk::g_launches.exchange(0) : cfk::g_launches.load();
 }
 
 extern "C" const char* cfk_version() { return "cfk_b200 0.1 (sm_100a)"; }

@@ -17,7 +17,11 @@ __device__ __forceinline__ void report_timeout(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// Every kernel launch of the library goes through check_launch(): it counts the launch (cfk_launch_count)
+// and turns a refused launch into a status.
+void note_launch();
 inline int check_launch() {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CFK_OK : CFK_ERR_LAUNCH;
 }

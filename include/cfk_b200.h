@@ -48,6 +48,10 @@ CFK_API const char* cfk_version(void);
  * handlers report through XLA's FFI error object). */
 CFK_API int cfk_last_device_status(int reset);
 
+/* Number of kernels this library has launched in this process (optionally reset to zero): lets a caller
+ * check that its work ran here and not in a fallback.  No reference counterpart. */
+CFK_API long long cfk_launch_count(int reset);
+
 /* ---- LayerNorm ------------------------------------------------------------------------------------
  * y = (x - mean) * rsqrt(var + eps) * scale + offset over the last axis, fp32 statistics.
  * x, y [m, c] in `dtype` (CFK_BF16 or CFK_F32); scale, offset [c] fp32.
