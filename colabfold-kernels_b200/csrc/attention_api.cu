@@ -11,7 +11,7 @@ bool attention_sm100_supported(const AttnProblem& p, int dtype);
 int attention_fwd_sm100(const AttnProblem& p, cudaStream_t st);
 bool attention_bwd_sm100_supported(const AttnBwdProblem& bp, int dtype);
 size_t attention_bwd_sm100_workspace(const AttnProblem& p);
-int attention_bwd_sm100(const AttnBwdProblem& bp, void* workspace, cudaStream_t st);
+int attention_bwd_sm100(const AttnBwdProblem& bp, float* delta, void* workspace, cudaStream_t st);
 
 namespace {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -121,8 +121,7 @@ extern "C" int cfk_attention_bwd(const void* q, const void* k, const void* v, co
   float* delta = static_cast<float*>(workspace);
   if (attention_bwd_sm100_supported(bp, dtype)) {
     char* rest = static_cast<char*>(workspace) + align_up(sizeof(float) * size_t(n) * h * sq, 256);
-    (void)delta;
-    return attention_bwd_sm100(bp, rest, st);
+    return attention_bwd_sm100(bp, delta, rest, st);
   }
   return attention_bwd_simt(bp, dtype, delta, st);
 }

@@ -296,6 +296,14 @@ int bwd_impl(const AttnBwdProblem& bp, float* delta, cudaStream_t st) {
 
 }  // namespace
 
+// delta[b,h,q] = sum_d out * dout for bf16 tensors (shared with the tcgen05 backward); the caller checks the launch
+void launch_attn_delta_bf16(const AttnBwdProblem& bp, float* delta, cudaStream_t st) {
+  const AttnProblem& p = bp.f;
+  const int64_t rows = int64_t(p.nb) * p.h * p.sq;
+  attn_delta_kernel<__nv_bfloat16><<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, st>>>(
+      p.out, p.so_, bp.dout, bp.sdo, delta, p.nb, p.h, p.sq, p.d);
+}
+
 int attention_fwd_simt(const AttnProblem& p, int dtype, cudaStream_t st) {
   if (p.d > kMaxD) return CFK_ERR_UNSUPPORTED;
   if (dtype == CFK_F32) return fwd_impl<float>(p, st);

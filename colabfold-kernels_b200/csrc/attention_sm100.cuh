@@ -36,7 +36,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Deadline-bounded mbarrier wait: polls until the phase flips or ~2^32 clocks have passed.
+// Deadline-bounded mbarrier wait: polls until the phase flips or ~2^30 clocks (about half a second) have passed.
 __device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
@@ -44,7 +44,7 @@ __device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parit
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > (1ll << 32)) return false;
+    if (clock64() - t0 > (1ll << 30)) return false;
   }
 }
 

@@ -139,3 +139,32 @@ def test_packed_bf16(case):
                                    column=column, trim=True)
   assert O.rel_err(out_t.cpu().float(), ref_t) <= BF16_TOL
   assert bool((out_t.cpu().float()[ref_t == 0] == 0).all())  # trimmed positions are exact zeros
+
+
+@pytest.mark.parametrize("shape", BF16_SHAPES + [(7, 2, 256, 384, 32)])
+@pytest.mark.parametrize("seq_major", [False, True])
+def test_bf16_backward(shape, seq_major):
+  """bf16 backward (tcgen05 kernel: dq, dk, dv in bf16, dbias in fp32): rel <= 2e-2 against the oracle's explicit
+  flash backward on the bf16-rounded inputs; a fully masked batch row differentiates the uniform softmax."""
+  from colabfold_kernels import ops
+  b, h, sq, sk, d = shape
+  q, k, v, bias, kmask, do = make_case(2, *shape, p_live=0.9, full_mask_row=b - 1 if b > 1 else None)
+  bf = lambda t: t.to(torch.bfloat16)
+  qb, kb, vb, bb, dob = bf(q), bf(k), bf(v), bf(bias), bf(do)
+  scale = d ** -0.5
+  tr = (lambda t: t.transpose(1, 2).contiguous()) if seq_major else (lambda t: t)
+  out, lse = ops.attention_fwd(dev(tr(qb)), dev(tr(kb)), dev(tr(vb)), dev(bb), dev(kmask), scale, seq_major=seq_major,
+                               want_lse=True)
+  dq, dk, dv, db = ops.attention_bwd(dev(tr(qb)), dev(tr(kb)), dev(tr(vb)), dev(bb), dev(kmask), out, dev(tr(dob)), lse,
+                                     scale, seq_major=seq_major)
+  assert ops.device_status() == 0
+  ref = O.ref_attn(qb, kb, vb, bb, kmask, scale)
+  lse_ref = O.ref_attn_lse(qb, kb, bb, kmask, scale)
+  rq, rk, rv, rb = O.ref_attn_bwd(qb, kb, vb, bb, kmask, ref, dob, lse_ref, scale)
+  un = (lambda t: t.cpu().float().transpose(1, 2)) if seq_major else (lambda t: t.cpu().float())
+  for name, a, r in (("dq", un(dq), rq), ("dk", un(dk), rk), ("dv", un(dv), rv), ("dbias", db.cpu(), rb)):
+    assert O.rel_err(a, r) <= BF16_TOL, name
+  # no dbias wanted: the other gradients are unchanged
+  dq2, dk2, dv2, none = ops.attention_bwd(dev(tr(qb)), dev(tr(kb)), dev(tr(vb)), dev(bb), dev(kmask), out, dev(tr(dob)),
+                                          lse, scale, seq_major=seq_major, want_dbias=False)
+  assert none is None and torch.equal(dk, dk2) and torch.equal(dv, dv2)
