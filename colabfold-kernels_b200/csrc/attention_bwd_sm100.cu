@@ -158,16 +158,16 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         constexpr uint32_t idesc_t = make_idesc(kBK, D, 1, 1, 1, 1);     // dV, dK: A = P^T / dS^T (MN-major), B MN-major
         constexpr uint32_t idesc_q = make_idesc(kBQ, D, 1, 1, 0, 1);     // dQ: A = dS (K-major), B = K (MN-major)
         constexpr uint32_t kTile16 = kTile >> 4;
-        const uint64_t q_k = desc_k_major(smem_u32(smem + kOffQ), kRowBytes);
-        const uint64_t do_k = desc_k_major(smem_u32(smem + kOffDo), kRowBytes);
-        const uint64_t k_k = desc_k_major(smem_u32(smem + kOffK), kRowBytes);
-        const uint64_t v_k = desc_k_major(smem_u32(smem + kOffV), kRowBytes);
-        const uint64_t q_mn = desc_mn_major(smem_u32(smem + kOffQ), kRowBytes, 0);
-        const uint64_t do_mn = desc_mn_major(smem_u32(smem + kOffDo), kRowBytes, 0);
-        const uint64_t k_mn = desc_mn_major(smem_u32(smem + kOffK), kRowBytes, 0);
-        const uint64_t p_mn = desc_mn_major(smem_u32(smem + kOffP), 128, kTileBig / 2);
-        const uint64_t ds_mn = desc_mn_major(smem_u32(smem + kOffDs), 128, kTileBig / 2);
-        const uint64_t ds_k = desc_k_major(smem_u32(smem + kOffDs), 128);
+        // low descriptor words (start address >> 4, leading byte offset); the high words are constants
+        constexpr uint32_t hi64 = desc_hi(8 * kRowBytes, kSwz64);   // Q, dO, K, V tiles: 64-byte rows
+        constexpr uint32_t hi128 = desc_hi(1024, kSwz128);          // P, dS tiles: 128-byte rows
+        const uint32_t q_k = desc_lo(smem_u32(smem + kOffQ), 16), do_k = desc_lo(smem_u32(smem + kOffDo), 16);
+        const uint32_t k_k = desc_lo(smem_u32(smem + kOffK), 16), v_k = desc_lo(smem_u32(smem + kOffV), 16);
+        const uint32_t q_mn = desc_lo(smem_u32(smem + kOffQ), 0), do_mn = desc_lo(smem_u32(smem + kOffDo), 0);
+        const uint32_t k_mn = desc_lo(smem_u32(smem + kOffK), 0);
+        const uint32_t p_mn = desc_lo(smem_u32(smem + kOffP), kTileBig / 2);
+        const uint32_t ds_mn = desc_lo(smem_u32(smem + kOffDs), kTileBig / 2);
+        const uint32_t ds_k = desc_lo(smem_u32(smem + kOffDs), 16);
         int s_g = 0, s_st = 0, o_g = 0, o_st = 0;
         uint32_t s_par = 0, s_first = 1, se_par = 1, pf_par = 0, o_first = 1;
         bool ok = true;
@@ -176,12 +176,12 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (!mbar_wait_deadline(&qdo_full[s_st], s_par)) { report_timeout(prm.status, 702); return false; }
           if (!mbar_wait_deadline(sdp_empty, se_par)) { report_timeout(prm.status, 703); return false; }
           tc_fence_after();
-          const uint64_t aq = q_k + uint64_t(s_st * kTile16), ad = do_k + uint64_t(s_st * kTile16);
-          const uint64_t bk = k_k + uint64_t(s_g * kTile16), bv = v_k + uint64_t(s_g * kTile16);
+          const uint32_t aq = q_k + s_st * kTile16, ad = do_k + s_st * kTile16;
+          const uint32_t bk = k_k + s_g * kTile16, bv = v_k + s_g * kTile16;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss(tmem + kColS, aq + 2 * kk, bk + 2 * kk, idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss2(tmem + kColS, aq + 2 * kk, hi64, bk + 2 * kk, hi64, idesc_s, kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss(tmem + kColDp, ad + 2 * kk, bv + 2 * kk, idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss2(tmem + kColDp, ad + 2 * kk, hi64, bv + 2 * kk, hi64, idesc_s, kk > 0);
           mma_commit(sdp_full);
           se_par ^= 1;
           if (++s_g == gcount) { s_g = 0; s_first = 0; }
@@ -191,23 +191,23 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         auto issue_out = [&]() {
           if (!mbar_wait_deadline(pds_full, pf_par)) { report_timeout(prm.status, 704); return false; }
           tc_fence_after();
-          const uint64_t bdo = do_mn + uint64_t(o_st * kTile16), bq = q_mn + uint64_t(o_st * kTile16);
-          const uint64_t bk = k_mn + uint64_t(o_g * kTile16);
+          const uint32_t bdo = do_mn + o_st * kTile16, bq = q_mn + o_st * kTile16;
+          const uint32_t bk = k_mn + o_g * kTile16;
           const uint32_t d_k = tmem + kColAcc + o_g * 64, d_v = d_k + 32;
           const uint32_t acc0 = o_first ^ 1;  // the first query block overwrites the dK/dV accumulators
           // dV_g += P^T dO and dK_g += dS^T Q: A MN-major, a K step is 16 query rows = 2048 bytes of P/dS,
           // 1024 bytes of dO/Q
 #pragma unroll
           for (int kk = 0; kk < kBQ / 16; ++kk)
-            mma_f16_ss(d_v, p_mn + uint64_t(kk * 128), bdo + uint64_t(kk * 64), idesc_t, kk > 0 ? 1u : acc0);
+            mma_f16_ss2(d_v, p_mn + kk * 128, hi128, bdo + kk * 64, hi64, idesc_t, kk > 0 ? 1u : acc0);
 #pragma unroll
           for (int kk = 0; kk < kBQ / 16; ++kk)
-            mma_f16_ss(d_k, ds_mn + uint64_t(kk * 128), bq + uint64_t(kk * 64), idesc_t, kk > 0 ? 1u : acc0);
+            mma_f16_ss2(d_k, ds_mn + kk * 128, hi128, bq + kk * 64, hi64, idesc_t, kk > 0 ? 1u : acc0);
           // dQ = dS K: A K-major (64 keys per 128-byte row, second half 16 KB on), a K step is 16 keys
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16_ss(tmem + kColDq, ds_k + uint64_t((kk / 4) * (kTileBig / 32) + (kk % 4) * 2), bk + uint64_t(kk * 64),
-                       idesc_q, kk > 0);
+            mma_f16_ss2(tmem + kColDq, ds_k + (kk / 4) * (kTileBig / 32) + (kk % 4) * 2, hi128, bk + kk * 64, hi64, idesc_q,
+                        kk > 0);
           mma_commit(&qdo_empty[o_st]);
           mma_commit(gemm_done);
           pf_par ^= 1;
@@ -249,7 +249,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     named_bar_sync(1, kSoftmaxThreads);
 
     const float scale = p.scale;
-    const float inv_sk = 1.0f / float(p.sk);
     float acc[64];  // dBias of this thread's (query row, 64 keys), summed over the G batch rows of a query block
     int t = 0;
     for (int i = 0; i < ni; ++i) {
@@ -269,17 +268,67 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         }
         CFK_BWD_WAIT(sdp_full, t & 1, 802)
         tc_fence_after();
-        float s[64], dp[64];
+        const float* madd = mask_all + g * 128 + half * 64;
+        const uint8_t* bias_tile = smem + kOffBias + half * (kTileBig / 2);
+        // a row whose keys were all masked: the forward was the uniform mean, so p = 1/Sk on every real key and
+        // ds = 0.  Handled by rewriting the inputs of the common formula (s := -mask so that s + mask = 0,
+        // lse := log2(Sk), dp := delta); whole batch rows are dead or alive, so the branch is warp-uniform.
+        const bool dead = lse <= kNegRef * 0.5f;
+        const bool any_dead = __any_sync(0xffffffffu, dead);
+        const float neg_lse = dead ? -__log2f(float(p.sk)) : -lse;
+        uint32_t pk[32], dk[32];
+        // two chunks of 32 keys keep the live registers (scores, dP, dBias sums, packed outputs) under the budget
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld_x32(tmem + lane_addr + kColS + half * 64 + c * 32, reinterpret_cast<uint32_t(&)[32]>(s[c * 32]));
-          tmem_ld_x32(tmem + lane_addr + kColDp + half * 64 + c * 32, reinterpret_cast<uint32_t(&)[32]>(dp[c * 32]));
+        for (int hc = 0; hc < 2; ++hc) {
+          float s[32], dp[32];
+          tmem_ld_x32(tmem + lane_addr + kColS + half * 64 + hc * 32, reinterpret_cast<uint32_t(&)[32]>(s));
+          tmem_ld_x32(tmem + lane_addr + kColDp + half * 64 + hc * 32, reinterpret_cast<uint32_t(&)[32]>(dp));
+          tmem_wait_ld();
+          if (hc == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sdp_empty);
+          }
+          if (prm.has_bias) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 w = *reinterpret_cast<const uint4*>(bias_tile + swz_off(row, hc * 4 + c, 128));
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                s[c * 8 + 2 * e] = fmaf(s[c * 8 + 2 * e], scale, bf16lo_to_f32(ww[e]));
+                s[c * 8 + 2 * e + 1] = fmaf(s[c * 8 + 2 * e + 1], scale, bf16hi_to_f32(ww[e]));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) s[c] *= scale;
+          }
+          if (any_dead) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const float a = madd[hc * 32 + c];
+              if (dead) {
+                s[c] = a == -INFINITY ? 0.f : -a;
+                dp[c] = dlt;
+              }
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 a = *reinterpret_cast<const float4*>(madd + hc * 32 + c * 4);
+            const float p0 = ex2_approx(fmaf(s[c * 4 + 0] + a.x, kLog2eF, neg_lse));
+            const float p1 = ex2_approx(fmaf(s[c * 4 + 1] + a.y, kLog2eF, neg_lse));
+            const float p2 = ex2_approx(fmaf(s[c * 4 + 2] + a.z, kLog2eF, neg_lse));
+            const float p3 = ex2_approx(fmaf(s[c * 4 + 3] + a.w, kLog2eF, neg_lse));
+            const float d0 = p0 * (dp[c * 4 + 0] - dlt), d1 = p1 * (dp[c * 4 + 1] - dlt);
+            const float d2 = p2 * (dp[c * 4 + 2] - dlt), d3 = p3 * (dp[c * 4 + 3] - dlt);
+            acc[hc * 32 + c * 4 + 0] += d0; acc[hc * 32 + c * 4 + 1] += d1;
+            acc[hc * 32 + c * 4 + 2] += d2; acc[hc * 32 + c * 4 + 3] += d3;
+            pk[hc * 16 + c * 2] = pack_bf16x2(p0, p1); pk[hc * 16 + c * 2 + 1] = pack_bf16x2(p2, p3);
+            dk[hc * 16 + c * 2] = pack_bf16x2(d0, d1); dk[hc * 16 + c * 2 + 1] = pack_bf16x2(d2, d3);
+          }
         }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sdp_empty);
-
         // the previous step's output GEMMs are complete: its dQ tile can leave TMEM, P/dS can be overwritten
         if (t > 0) {
           CFK_BWD_WAIT(gemm_done, (t - 1) & 1, 803)
@@ -293,59 +342,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             *reinterpret_cast<float4*>(stg + c * 4) =
                 make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
                             __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
-        }
-
-        // logits, probabilities, score gradients for this thread's 64 keys
-        if (prm.has_bias) {
-          const uint8_t* bias_tile = smem + kOffBias + half * (kTileBig / 2);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 w = *reinterpret_cast<const uint4*>(bias_tile + swz_off(row, c, 128));
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              s[c * 8 + 2 * e] = fmaf(s[c * 8 + 2 * e], scale, bf16lo_to_f32(ww[e]));
-              s[c * 8 + 2 * e + 1] = fmaf(s[c * 8 + 2 * e + 1], scale, bf16hi_to_f32(ww[e]));
-            }
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) s[c] *= scale;
-        }
-        const float* madd = mask_all + g * 128 + half * 64;
-        const bool dead = lse <= kNegRef * 0.5f;  // a row whose keys were all masked: the forward was the uniform mean
-        uint32_t pk[32], dk[32];
-        if (!__any_sync(0xffffffffu, dead)) {
-          const float neg_lse = -lse;
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float4 a = *reinterpret_cast<const float4*>(madd + c * 4);
-            const float p0 = ex2_approx(fmaf(s[c * 4 + 0] + a.x, kLog2eF, neg_lse));
-            const float p1 = ex2_approx(fmaf(s[c * 4 + 1] + a.y, kLog2eF, neg_lse));
-            const float p2 = ex2_approx(fmaf(s[c * 4 + 2] + a.z, kLog2eF, neg_lse));
-            const float p3 = ex2_approx(fmaf(s[c * 4 + 3] + a.w, kLog2eF, neg_lse));
-            const float d0 = p0 * (dp[c * 4 + 0] - dlt), d1 = p1 * (dp[c * 4 + 1] - dlt);
-            const float d2 = p2 * (dp[c * 4 + 2] - dlt), d3 = p3 * (dp[c * 4 + 3] - dlt);
-            acc[c * 4 + 0] += d0; acc[c * 4 + 1] += d1; acc[c * 4 + 2] += d2; acc[c * 4 + 3] += d3;
-            pk[c * 2] = pack_bf16x2(p0, p1); pk[c * 2 + 1] = pack_bf16x2(p2, p3);
-            dk[c * 2] = pack_bf16x2(d0, d1); dk[c * 2 + 1] = pack_bf16x2(d2, d3);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float a0 = madd[2 * c], a1 = madd[2 * c + 1];
-            float p0, p1, d0, d1;
-            if (dead) {
-              p0 = a0 == -INFINITY ? 0.f : inv_sk; p1 = a1 == -INFINITY ? 0.f : inv_sk;
-              d0 = d1 = 0.f;
-            } else {
-              p0 = ex2_approx(fmaf(s[2 * c] + a0, kLog2eF, -lse)); p1 = ex2_approx(fmaf(s[2 * c + 1] + a1, kLog2eF, -lse));
-              d0 = p0 * (dp[2 * c] - dlt); d1 = p1 * (dp[2 * c + 1] - dlt);
-            }
-            acc[2 * c] += d0; acc[2 * c + 1] += d1;
-            pk[c] = pack_bf16x2(p0, p1);
-            dk[c] = pack_bf16x2(d0, d1);
-          }
         }
         // P and dS rows into shared memory (64 keys = one 128-byte swizzled row of this thread's half)
         uint8_t* p_row = smem + kOffP + half * (kTileBig / 2);
