@@ -55,3 +55,129 @@ class _LayerNorm(torch.autograd.Function):
 
 def layer_norm(x, scale, offset, *, eps=1e-5):
   return _LayerNorm.apply(x, scale, offset, float(eps))
+
+
+# ---- forward-only kernels, backward through the differentiable reference (grads.py:106-143) -----------------
+def differentiable_via(fwd, ref, nondiff=()):
+  """fwd's forward with the gradient of ref, which recomputes in the backward.  fwd and ref take the same
+  arguments; keyword arguments must be named in `nondiff` (they are static); integral or absent positional
+  inputs get no gradient."""
+
+  def call(*args, **kwargs):
+    extra = set(kwargs) - set(nondiff)
+    if extra:
+      raise TypeError(f"{getattr(fwd, '__name__', fwd)}: pass {sorted(extra)} positionally")
+    diff = [i for i, a in enumerate(args) if torch.is_tensor(a) and a.is_floating_point() and a.requires_grad]
+    if not diff or not torch.is_grad_enabled():
+      return fwd(*args, **kwargs)
+    return _Via.apply(fwd, ref, kwargs, diff, len(args), *args)
+
+  call.__name__ = getattr(fwd, "__name__", "fused")
+  call.__doc__ = fwd.__doc__
+  return call
+
+
+class _Via(torch.autograd.Function):
+
+  @staticmethod
+  def forward(ctx, fwd, ref, kwargs, diff, nargs, *args):
+    ctx.ref, ctx.kwargs, ctx.diff = ref, kwargs, diff
+    ctx.args = args
+    out = fwd(*[a.detach() if torch.is_tensor(a) else a for a in args], **kwargs)
+    ctx.tuple_out = isinstance(out, (tuple, list))
+    return tuple(out) if ctx.tuple_out else out
+
+  @staticmethod
+  def backward(ctx, *douts):
+    args = list(ctx.args)
+    leaves = []
+    for i in ctx.diff:
+      leaf = args[i].detach().requires_grad_(True)
+      args[i] = leaf
+      leaves.append(leaf)
+    with torch.enable_grad():
+      out = ctx.ref(*args, **ctx.kwargs)
+      outs = out if isinstance(out, (tuple, list)) else (out,)
+      pairs = [(o, d) for o, d in zip(outs, douts) if o is not None and d is not None]
+      loss = sum((o.float() * d.float()).sum() for o, d in pairs)
+    grads = torch.autograd.grad(loss, leaves, allow_unused=True)
+    full = [None] * len(ctx.args)
+    for i, g in zip(ctx.diff, grads):
+      full[i] = None if g is None else g.to(ctx.args[i].dtype)
+    return (None, None, None, None, None, *full)
+
+
+# ---- gated dual projection (grads.py:56-102): the two projections are recomputed in the backward -------------
+class _Gdp(torch.autograd.Function):
+
+  @staticmethod
+  def forward(ctx, x, wp, bp, wg, bg, mask, split, channel_major, activation):
+    ctx.save_for_backward(x, wp, bp, wg, bg, mask)
+    ctx.cfg = (split, channel_major, activation)
+    out = ops.gated_dual_proj(x, wp, bp, wg, bg, mask, split=split, channel_major=channel_major, activation=activation)
+    return out
+
+  @staticmethod
+  def backward(ctx, *dys):
+    x, wp, bp, wg, bg, mask = ctx.saved_tensors
+    split, channel_major, activation = ctx.cfg
+    if split:
+      left, right = (t.T for t in dys) if channel_major else dys
+      dy = torch.cat([left, right], dim=-1)
+    else:
+      dy = dys[0]
+    xf, dyf = x.float(), dy.float()
+    proj = xf @ wp.float() + bp.float()
+    gate = (xf @ wg.float() + bg.float()).detach().requires_grad_(True)
+    with torch.enable_grad():
+      act = torch.nn.functional.silu(gate) if activation == 1 else torch.sigmoid(gate)
+    m = mask.float()[:, None]
+    dproj = dyf * m * act.detach()
+    dgate, = torch.autograd.grad(act, gate, dyf * m * proj)
+    dx = dproj @ wp.float().T + dgate @ wg.float().T
+    dmask = (dyf * proj * act.detach()).sum(-1).to(mask.dtype) if mask.is_floating_point() else None
+    return (dx.to(x.dtype), (xf.T @ dproj).to(wp.dtype), dproj.sum(0).to(bp.dtype), (xf.T @ dgate).to(wg.dtype),
+            dgate.sum(0).to(bg.dtype), dmask, None, None, None)
+
+
+def gated_dual_proj(x, wp, bp, wg, bg, mask, *, split=False, channel_major=False, activation=0):
+  return _Gdp.apply(x, wp, bp, wg, bg, mask, bool(split), bool(channel_major), int(activation))
+
+
+# ---- packed attention: forward reads p in place, backward is the flash backward on the unpacked slots ----------
+class _PackedAttention(torch.autograd.Function):
+  """packed_attn.py:163-177 `attention_via`: the VJP is that of attention on the unpacked slots followed by the gate."""
+
+  @staticmethod
+  def forward(ctx, p, bias, kmask, gate_bias, sm_scale, column, trim):
+    ctx.save_for_backward(p, bias if bias is not None else torch.empty(0, device=p.device), kmask,
+                          gate_bias if gate_bias is not None else torch.empty(0, device=p.device))
+    ctx.cfg = (sm_scale, column, trim, bias is not None, gate_bias is not None)
+    return ops.packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=column, trim=trim)
+
+  @staticmethod
+  def backward(ctx, dout):
+    p, bias, kmask, gate_bias = ctx.saved_tensors
+    sm_scale, column, trim, has_bias, gated = ctx.cfg
+    bias = bias if has_bias else None
+    pp = p.transpose(0, 1) if column else p              # [batch, seq, G, H, D]
+    do = dout.transpose(0, 1) if column else dout
+    q, k, v = (pp[:, :, i].contiguous() for i in range(3))  # seq-major [b, s, h, d]
+    o_att, lse = ops.attention_fwd(q, k, v, bias, kmask, sm_scale, seq_major=True, want_lse=True)
+    do = do.contiguous()
+    dg = None
+    if gated:
+      sig = torch.sigmoid(pp[:, :, 3].float() + gate_bias.float())
+      dg = do.float() * o_att.float() * sig * (1 - sig)
+      do = (do.float() * sig).to(p.dtype)
+    dq, dk, dv, dbias = ops.attention_bwd(q, k, v, bias, kmask, o_att, do, lse, sm_scale, seq_major=True,
+                                          want_dbias=has_bias)
+    parts = [dq, dk, dv] + ([dg.to(p.dtype)] if gated else [])
+    dp = torch.stack(parts, dim=2)
+    dp = dp.transpose(0, 1) if column else dp
+    return (dp.contiguous(), dbias.to(bias.dtype) if has_bias else None, None,
+            dg.sum(dim=(0, 1)).to(gate_bias.dtype) if gated else None, None, None, None)
+
+
+def packed_attention(p, bias, kmask, gate_bias=None, *, sm_scale, column=False, trim=False):
+  return _PackedAttention.apply(p, bias, kmask, gate_bias, float(sm_scale), bool(column), bool(trim))

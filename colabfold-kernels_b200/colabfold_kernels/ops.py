@@ -145,3 +145,117 @@ def contract(a, b, alpha=1.0):
   with torch.cuda.device(a.device):
     _lib.call("cfk_contract", _ptr(a), _ptr(b), _ptr(out), c, i, j, k, tag(a.dtype), float(alpha), _stream())
   return out
+
+
+# ------------------------------------------------------------------------------------------ projection family
+def _f32(t):
+  return _c(t.float())
+
+
+def gated_dual_proj(x, wp, bp, wg, bg, mask, split=False, channel_major=False, activation=0):
+  """mask * (x wp + bp) * act(x wg + bg); bf16.  -> [m,p], or (left, right) each [m,p/2] / [p/2,m]."""
+  x = _c(x)
+  m, k = x.shape
+  p = wp.shape[1]
+  dt = x.dtype
+  if split:
+    shape = (p // 2, m) if channel_major else (m, p // 2)
+    out0, out1 = torch.empty(shape, dtype=dt, device=x.device), torch.empty(shape, dtype=dt, device=x.device)
+  else:
+    out0, out1 = torch.empty((m, p), dtype=dt, device=x.device), None
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_gated_dual_proj", _ptr(x), _ptr(_c(wp.to(dt))), _ptr(_c(bp.to(dt))), _ptr(_c(wg.to(dt))),
+              _ptr(_c(bg.to(dt))), _ptr(_c(mask.to(dt))), _ptr(out0), _ptr(out1), m, k, p, int(split),
+              int(channel_major), int(activation), _stream())
+  return (out0, out1) if split else out0
+
+
+def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, transpose=False, pad=1, fp8=False):
+  """-> left, right channel-major: [p/2, m'] for x [m,k], [p/2, a, b'] / [p/2, b, a'] for the pair x [a,b,k]."""
+  x = _c(x)
+  dt = x.dtype
+  k, p = x.shape[-1], wp.shape[1]
+  ci = p // 2
+  if x.ndim == 3:
+    a, b = x.shape[0], x.shape[1]
+    outer, inner = (b, a) if transpose else (a, b)
+    shape = (ci, outer, -(-inner // pad) * pad)
+  else:
+    a, b = x.shape[0], 0
+    shape = (ci, -(-a // pad) * pad)
+  odt = torch.float8_e4m3fn if fp8 else dt
+  left, right = torch.empty(shape, dtype=odt, device=x.device), torch.empty(shape, dtype=odt, device=x.device)
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_ln_gated_dual_proj", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(wp.to(dt))),
+              _ptr(_c(bp.to(dt))), _ptr(_c(wg.to(dt))), _ptr(_c(bg.to(dt))), _ptr(_c(mask.to(dt))), _ptr(left),
+              _ptr(right), a, b, k, p, int(transpose), int(pad), int(fp8), float(eps), _stream())
+  return left, right
+
+
+def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, in_scale=None, in_offset=None,
+                    eps=1e-5, add_input=False, out=None):
+  """(LN(x_cm^T) wo + bo) * sigmoid(g wg + bg) (+ residual | + act); g = act, or LN(act) when in_scale is given."""
+  act = _c(act)
+  x_cm = _c(x_cm if x_cm.dtype in (torch.bfloat16, torch.float32) else x_cm.to(torch.bfloat16))
+  dt = act.dtype
+  c, m = x_cm.shape
+  ca, o = act.shape[1], wo.shape[1]
+  if out is None:
+    out = torch.empty((m, o), dtype=dt, device=act.device)
+  res = None if residual is None else _c(residual.to(dt))
+  with torch.cuda.device(act.device):
+    _lib.call("cfk_trimul_epilogue", _ptr(x_cm), tag(x_cm.dtype), _ptr(act),
+              _ptr(None if in_scale is None else _f32(in_scale)), _ptr(None if in_offset is None else _f32(in_offset)),
+              _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(wo.to(dt))), _ptr(_c(bo.to(dt))), _ptr(_c(wg.to(dt))),
+              _ptr(_c(bg.to(dt))), _ptr(res), _ptr(out), m, c, ca, o, float(eps), int(add_input), _stream())
+  return out
+
+
+def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f8_scale=1.0):
+  """-> (p [m, g*n] or None, bias [h, m] or None)."""
+  x = _c(x)
+  dt = x.dtype
+  m, a = x.shape
+  p_out = b_out = None
+  with torch.cuda.device(x.device):
+    if w is not None:
+      g, _, n = w.shape
+      p_out = torch.empty((m, g * n), dtype=torch.float8_e4m3fn if f8 else dt, device=x.device)
+      _lib.call("cfk_ln_projection", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w.to(dt))),
+                _ptr(p_out), m, a, g, n, int(f8), float(f8_scale), float(eps), _stream())
+    if wb is not None:
+      h = wb.shape[1]
+      hp = -(-h // 8) * 8
+      wbp = torch.nn.functional.pad(wb.to(dt), (0, hp - h)).contiguous()
+      b_out = torch.empty((h, m), dtype=dt, device=x.device)
+      _lib.call("cfk_ln_head_bias", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(wbp), _ptr(b_out), m, a,
+                h, hp, float(eps), _stream())
+  return p_out, b_out
+
+
+def output_projection(o, w, b, residual=None, out=None):
+  o = _c(o)
+  dt = o.dtype
+  m, k = o.shape
+  c = w.shape[1]
+  res = None if residual is None else _c(residual.to(dt))
+  if out is None:
+    out = torch.empty((m, c), dtype=dt, device=o.device)
+  with torch.cuda.device(o.device):
+    _lib.call("cfk_output_projection", _ptr(o), _ptr(_c(w.to(dt))), _ptr(_c(b.to(dt))), _ptr(res), _ptr(out), m, k, c,
+              _stream())
+  return out
+
+
+def opm_projection(x, ln_scale, ln_offset, lw, lb, rw, rb, mask, eps=1e-5):
+  x = _c(x)
+  dt = x.dtype
+  c, k = x.shape[-1], lw.shape[1]
+  m = x.numel() // c
+  left = torch.empty(x.shape[:-1] + (k,), dtype=dt, device=x.device)
+  right = torch.empty_like(left)
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_opm_projection", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(lw.to(dt))),
+              _ptr(_c(lb.to(dt))), _ptr(_c(rw.to(dt))), _ptr(_c(rb.to(dt))), _ptr(_c(mask.to(dt))), _ptr(left),
+              _ptr(right), m, c, k, float(eps), _stream())
+  return left, right

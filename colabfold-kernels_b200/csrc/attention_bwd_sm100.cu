@@ -133,13 +133,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         int step = 0;
         bool ok = true;
         for (int i = 0; i < ni && ok; ++i) {
-          if (prm.has_bias) {
-            ok = mbar_wait_deadline(bias_empty, (i & 1) ^ 1);
-            if (!ok) { report_timeout(prm.status, 601); break; }
-            mbar_arrive_expect_tx(bias_full, kTileBig);
-            tma_load_3d(smem + kOffBias, &tm_bias, bias_full, k0, i * kBQ, head);
-            tma_load_3d(smem + kOffBias + kTileBig / 2, &tm_bias, bias_full, k0 + 64, i * kBQ, head);
-          }
           for (int g = 0; g < gcount; ++g, ++step) {
             const int st = step % kQdoStages;
             ok = mbar_wait_deadline(&qdo_empty[st], ((step / kQdoStages) & 1) ^ 1);
@@ -148,6 +141,18 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             tma_load_4d(smem + kOffQ + st * kTile, &tm_q, &qdo_full[st], 0, i * kBQ, head, b0 + g);
             tma_load_4d(smem + kOffDo + st * kTile, &tm_do, &qdo_full[st], 0, i * kBQ, head, b0 + g);
           }
+        }
+      }
+      __syncwarp();
+    } else if (warp == 3) {
+      // ---------------------------------------------------------------- TMA producer: bias tile per query block
+      // (its own warp, so that waiting for the single bias buffer never holds back the Q / dO prefetch)
+      if (lane == 0 && prm.has_bias) {
+        for (int i = 0; i < ni; ++i) {
+          if (!mbar_wait_deadline(bias_empty, (i & 1) ^ 1)) { report_timeout(prm.status, 601); break; }
+          mbar_arrive_expect_tx(bias_full, kTileBig);
+          tma_load_3d(smem + kOffBias, &tm_bias, bias_full, k0, i * kBQ, head);
+          tma_load_3d(smem + kOffBias + kTileBig / 2, &tm_bias, bias_full, k0 + 64, i * kBQ, head);
         }
       }
       __syncwarp();

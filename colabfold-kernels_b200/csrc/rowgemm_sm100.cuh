@@ -1,0 +1,67 @@
+// Row-block GEMM with fused prologue and epilogue: the shared engine of the HBM-bound projection kernels
+// (gated dual projection, LayerNorm -> gated dual projection, triangle-multiplication epilogue, LayerNorm ->
+// packed projection, output projection, outer-product-mean projection).
+//
+// A persistent CTA walks 128-row tiles.  Per tile:
+//   prologue warps (4)  one thread per row: load the row (row-major source, optionally through a pair transpose,
+//                       or a channel-major source), LayerNorm it in fp32 registers, round to bf16 and write it as a
+//                       128-byte-swizzled K-major UMMA operand into one of two shared-memory stages
+//   MMA issuer          for every 128-column chunk of the output: acc0 = A0 W0 (and acc1 = A1 W1) with the
+//                       weights resident in shared memory in their natural [K, N] layout (MN-major B operand)
+//   epilogue warps (4)  TMEM -> registers -> bias / activation / mask / residual -> bf16 (or e4m3) -> global
+//                       (row-major: straight from registers; channel-major: transposed through shared memory
+//                       and written by TMA)
+#pragma once
+#include "attention_sm100.cuh"
+
+namespace cfk {
+
+enum RowGemmMode : int {
+  kModeLinear = 0,  // out_i = rowmask * (acc_i + b_i) (+ residual)        (one or two independent outputs)
+  kModeGdp = 1,     // out = rowmask * (acc0 + b0) * act(acc1 + b1)
+  kModeEpi = 2,     // out = (acc0 + b0) * sigmoid(acc1 + b1) (+ residual | + raw rows of source 1)
+};
+
+struct RowSource {
+  const void* x;           // nullptr: unused (source 1 then shares source 0's tile)
+  const float* ln_scale;   // nullptr: no LayerNorm
+  const float* ln_offset;
+  int64_t stride_outer;    // row index of (outer o, inner r) = o * stride_outer + r * stride_inner   (row-major source)
+  int64_t stride_inner;
+  int channel_major;       // 1: x is [K, rows] (bf16 or fp32), rows indexed o * inner + r
+  int dtype;               // CFK_BF16 / CFK_F32 (fp32 only for a channel-major source)
+  int k;                   // 64, 128 or 256
+};
+
+struct RowGemmParams {
+  RowSource src[2];
+  int64_t outer, inner, inner_pad;  // tiles = outer * ceil(inner_pad / 128); rows r >= inner are zero padding
+  float eps;
+  int mode, swish;                  // swish: act = x * sigmoid(x) instead of sigmoid (GDP only)
+  int dual;                         // two accumulators per chunk
+  int n_chunk;                      // columns per accumulator and chunk: 16..128, multiple of 16
+  int chunks;                       // chunks handled per tile (weights of all of them stay resident)
+  int chunk0;                       // global index of this launch's first chunk (launches may split the chunk list)
+  int chunks_per_slot;              // global chunk c -> weight slot c / chunks_per_slot, column (c % chunks_per_slot) * n_chunk
+  int bias_slot_stride;             // bias index = slot * bias_slot_stride + column
+  const void* bias[2];              // bf16 [N] per accumulator or nullptr (indexed by absolute output column)
+  const void* rowmask;              // [rows] in src[0] order (bf16 or fp32 by rowmask_dtype) or nullptr
+  int rowmask_dtype;
+  // row-major output: out[i][row * ldo + col0[i] + chunk columns]; chunk c of accumulator i lands in array
+  // (c / chunks_per_array), column (c % chunks_per_array) * n_chunk
+  void* out[2];
+  int64_t ldo;
+  int chunks_per_array;
+  int out_dtype;                    // CFK_BF16 or CFK_E4M3 (saturating, times out_scale)
+  float out_scale;
+  int out_channel_major;            // 1: out[array] is [n, outer, inner_pad] (lanes store consecutive rows of a channel)
+  int n_valid;                      // real columns per array (columns past it are not stored)
+  const void* residual;             // row-major [rows, ldo] (same dtype as out) or nullptr
+  int add_source1;                  // kModeEpi: add the raw rows of source 1
+  int* status;
+};
+
+int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st);
+int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
+
+}  // namespace cfk

@@ -1,0 +1,141 @@
+"""The projection family on the GPU (row-block tcgen05 GEMM engine) against the CPU oracle: shapes and
+tolerances of tests/test_ln_gdp_grad.py:58-59,75, tests/test_ln_fusions.py:38,127-138 and
+tests/test_af2_fused_kernels.py:90-91 restricted to the widths this build takes (K in {64,128,256})."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 3e-2  # the reference's bound for the fused projections (tests/test_af2_fused_kernels.py:22)
+bf = torch.bfloat16
+
+
+def rnd(rng, *shape, s=.5):
+  return torch.from_numpy((rng.standard_normal(shape) * s).astype(np.float32)).to(bf)
+
+
+def chk(got, ref, tol=TOL):
+  err = O.rel_err(got.cpu().float(), ref)
+  assert err <= tol, err
+
+
+@pytest.mark.parametrize("m,k,p,split,cm", [(2048, 128, 256, False, False), (2048, 128, 256, True, False),
+                                            (2048, 128, 256, True, True), (999, 64, 128, True, True), (1, 128, 256, False, False),
+                                            (300, 256, 128, True, False)])
+@pytest.mark.parametrize("act", [0, 1])
+def test_gated_dual_proj(m, k, p, split, cm, act):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(0)
+  x, wp, bp, wg, bg = rnd(rng, m, k), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1)
+  mask = torch.from_numpy((rng.random(m) > .1).astype(np.float32)).to(bf)
+  ref = O.ref_gdp(x, wp, bp, wg, bg, mask, activation="swish" if act else "sigmoid")
+  out = ops.gated_dual_proj(x.cuda(), wp.cuda(), bp.cuda(), wg.cuda(), bg.cuda(), mask.cuda(), split=split,
+                            channel_major=cm, activation=act)
+  assert ops.device_status() == 0
+  if not split:
+    chk(out, ref)
+  else:
+    l, r = ref[:, :p // 2], ref[:, p // 2:]
+    chk(out[0], l.T if cm else l)
+    chk(out[1], r.T if cm else r)
+
+
+@pytest.mark.parametrize("m", [1, 59, 4101, 260 * 260])
+def test_ln_gdp_2d_and_fused_equals_unfused(m):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(1)
+  k, p = 128, 256
+  x, wp, bp, wg, bg = rnd(rng, m, k), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1)
+  sc = 1 + rnd(rng, k, s=.1).float()
+  of = rnd(rng, k, s=.1).float()
+  mask = torch.from_numpy((rng.random(m) > .1).astype(np.float32)).to(bf)
+  l, r = ops.ln_gated_dual_proj(x.cuda(), sc.cuda(), of.cuda(), wp.cuda(), bp.cuda(), wg.cuda(), bg.cuda(), mask.cuda())
+  assert ops.device_status() == 0
+  rl, rr = O.ref_ln_gdp(x, sc, of, wp, bp, wg, bg, mask)
+  chk(l, rl); chk(r, rr)
+  # fused == LayerNorm kernel followed by the gated dual projection kernel (tests/test_ln_fusions.py:127-138)
+  y = ops.layer_norm(x.cuda(), sc.cuda(), of.cuda())
+  ul, ur = ops.gated_dual_proj(y, wp.cuda(), bp.cuda(), wg.cuda(), bg.cuda(), mask.cuda(), split=True, channel_major=True)
+  assert O.rel_err(l.cpu().float(), ul.cpu().float()) <= 1e-2
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_ln_gdp_pair(transpose, fp8):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(2)
+  a, b, k, p = 70, 150, 128, 256
+  x, wp, bp, wg, bg = rnd(rng, a, b, k), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1)
+  sc, of = 1 + rnd(rng, k, s=.1).float(), rnd(rng, k, s=.1).float()
+  mask = torch.from_numpy((rng.random((a, b)) > .1).astype(np.float32)).to(bf)
+  mask[3] = -1  # negative mask values count as zero
+  l, r = ops.ln_gated_dual_proj(x.cuda(), sc.cuda(), of.cuda(), wp.cuda(), bp.cuda(), wg.cuda(), bg.cuda(), mask.cuda(),
+                                transpose=transpose, pad=16, fp8=fp8)
+  assert ops.device_status() == 0
+  rl, rr = O.ref_ln_gdp(x, sc, of, wp, bp, wg, bg, mask, transpose=transpose, pad=16)
+  assert tuple(l.shape) == tuple(rl.shape)
+  if fp8:
+    assert O.rms_err(l.cpu().float(), rl) <= 5e-2 and O.rms_err(r.cpu().float(), rr) <= 5e-2
+  else:
+    chk(l, rl); chk(r, rr)
+  # the zero padding of the contracted axis is exact
+  inner = a if transpose else b
+  assert float(l.cpu().float()[..., inner:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("m,c,xdt", [(4096, 128, bf), (999, 128, bf), (500, 64, bf), (1, 128, bf), (127, 128, bf),
+                                     (999, 128, torch.float32)])
+def test_trimul_epilogue(m, c, xdt):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(3)
+  x_cm, act = rnd(rng, c, m).to(xdt), rnd(rng, m, c)
+  sc, of = 1 + rnd(rng, c, s=.1).float(), rnd(rng, c, s=.1).float()
+  wo, bo, wg, bg = rnd(rng, c, c, s=c ** -.5), rnd(rng, c, s=.1), rnd(rng, c, c, s=c ** -.5), rnd(rng, c, s=.1)
+  res = rnd(rng, m, c)
+  args = (x_cm.cuda(), act.cuda(), sc.cuda(), of.cuda(), wo.cuda(), bo.cuda(), wg.cuda(), bg.cuda())
+  chk(ops.trimul_epilogue(*args), O.ref_trimul_epilogue(x_cm, act, sc, of, wo, bo, wg, bg))
+  chk(ops.trimul_epilogue(*args, residual=res.cuda()), O.ref_trimul_epilogue(x_cm, act, sc, of, wo, bo, wg, bg, res))
+  isc, iof = 1 + rnd(rng, c, s=.1).float(), rnd(rng, c, s=.1).float()
+  got = ops.trimul_epilogue(*args, in_scale=isc.cuda(), in_offset=iof.cuda(), add_input=True)
+  chk(got, O.ref_trimul_epilogue_ln(x_cm, act, isc, iof, sc, of, wo, bo, wg, bg, add_input=True))
+  assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("m,a,g,n,h", [(4101, 128, 4, 128, 4), (59, 64, 4, 64, 4), (1000, 256, 4, 256, 8), (1, 128, 3, 128, 4)])
+def test_ln_projection(m, a, g, n, h):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(4)
+  x, w, wb = rnd(rng, m, a), rnd(rng, g, a, n, s=a ** -.5), rnd(rng, a, h, s=a ** -.5)
+  sc, of = 1 + rnd(rng, a, s=.1).float(), rnd(rng, a, s=.1).float()
+  p, b = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), wb.cuda())
+  assert ops.device_status() == 0
+  rp, rb = O.ref_ln_projection(x, sc, of, w, wb)
+  chk(p, rp); chk(b, rb)
+  p8, _ = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), None, f8=True, f8_scale=0.5)
+  assert O.rms_err(p8.cpu().float(), rp * 0.5) <= 5e-2  # tests/test_ln_fusions.py:192
+
+
+@pytest.mark.parametrize("m,k,c", [(4101, 128, 128), (59, 64, 64), (1000, 256, 256), (1, 128, 256)])
+def test_output_projection(m, k, c):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(5)
+  o, w, b, res = rnd(rng, m, k), rnd(rng, k, c, s=k ** -.5), rnd(rng, c, s=.1), rnd(rng, m, c)
+  chk(ops.output_projection(o.cuda(), w.cuda(), b.cuda()), O.ref_output_projection(o, w, b))
+  chk(ops.output_projection(o.cuda(), w.cuda(), b.cuda(), res.cuda()), O.ref_output_projection(o, w, b, res))
+  assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("s,r,c,k", [(6, 10, 64, 16), (64, 100, 256, 32), (3, 300, 128, 32)])
+def test_opm_projection(s, r, c, k):
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(6)
+  x = rnd(rng, s, r, c)
+  sc, of = 1 + rnd(rng, c, s=.1).float(), rnd(rng, c, s=.1).float()
+  lw, lb, rw, rb = rnd(rng, c, k, s=c ** -.5), rnd(rng, k, s=.1), rnd(rng, c, k, s=c ** -.5), rnd(rng, k, s=.1)
+  mask = torch.from_numpy((rng.random((s, r)) > .1).astype(np.float32)).to(bf)
+  l, rr = ops.opm_projection(x.cuda(), sc.cuda(), of.cuda(), lw.cuda(), lb.cuda(), rw.cuda(), rb.cuda(), mask.cuda())
+  assert ops.device_status() == 0
+  rl, rrr = O.ref_opm_projection(x, sc, of, lw, lb, rw, rb, mask)
+  chk(l, rl); chk(rr, rrr)
