@@ -1,0 +1,213 @@
+"""One AlphaFold2 Evoformer block composed from the fused ops, on one GPU or row-sharded over P GPUs.
+
+The block wiring is not part of colabfold-kernels (it lives in ColabFold/AlphaFold); this module composes the
+reference's ops in the published Evoformer order - MSA row attention with pair bias, MSA column attention, MSA
+transition, outer product mean, triangle multiplication outgoing and incoming, triangle attention starting and
+ending node, pair transition - each a residual update, inference mode (no dropout).
+
+`block(...)` runs on one device.  `ShardedBlock` keeps the MSA sharded over sequences (or residues) and the pair
+representation sharded over rows, one process per GPU: every op works on its local shard, all-to-all switches an
+operand between row and column sharding, all-gather supplies what every rank needs whole (the shared attention
+biases, the right-hand operand of the triangle contraction, the right outer-product projection).  The kernels
+only ever read local memory.
+
+Every function takes the namespace `K` that supplies the ops: `cuda_kernels()` (the C library) in production; the
+CPU tests pass one built on the oracle so that the sharding logic can be checked with the gloo backend.
+"""
+import math
+import types
+
+import torch
+
+
+def init_params(c_m=256, c_z=128, heads_msa=8, heads_pair=4, d_head=32, c_opm=32, c_tri=128, factor=4, seed=0,
+                dtype=torch.bfloat16, device="cpu"):
+  """Random-init weights of one block (Xavier-normal matrices, zero biases, LayerNorm scale 1 / offset 0)."""
+  g = torch.Generator().manual_seed(seed)
+
+  def xav(*shape):
+    fan_in, fan_out = shape[-2], shape[-1]
+    return (torch.randn(*shape, generator=g) * math.sqrt(2.0 / (fan_in + fan_out))).to(dtype).to(device)
+
+  def zeros(*shape):
+    return torch.zeros(*shape, dtype=dtype, device=device)
+
+  def ln(c):
+    return torch.ones(c, dtype=torch.float32, device=device), torch.zeros(c, dtype=torch.float32, device=device)
+
+  def attn(c, heads, bias_from=None):
+    d = {"ln": ln(c), "w": xav(4, c, heads * d_head), "gate_bias": zeros(heads, d_head).add_(1.0),
+         "wo": xav(heads * d_head, c), "bo": zeros(c), "heads": heads}
+    if bias_from is not None:
+      d["bias_ln"], d["wb"] = ln(bias_from), xav(bias_from, heads)
+    return d
+
+  def trans(c):
+    return {"ln": ln(c), "w1": xav(c, factor * c), "b1": zeros(factor * c), "w2": xav(factor * c, c), "b2": zeros(c)}
+
+  def trimul():
+    return {"ln": ln(c_z), "wp": xav(c_z, 2 * c_tri), "bp": zeros(2 * c_tri), "wg": xav(c_z, 2 * c_tri),
+            "bg": zeros(2 * c_tri).add_(1.0), "center_ln": ln(c_tri), "wo": xav(c_tri, c_z), "bo": zeros(c_z),
+            "wgo": xav(c_z, c_z), "bgo": zeros(c_z).add_(1.0)}
+
+  return {
+      "row_attn": attn(c_m, heads_msa, bias_from=c_z), "col_attn": attn(c_m, heads_msa), "msa_transition": trans(c_m),
+      "opm": {"ln": ln(c_m), "lw": xav(c_m, c_opm), "lb": zeros(c_opm), "rw": xav(c_m, c_opm), "rb": zeros(c_opm),
+              "w": xav(c_opm * c_opm, c_z), "b": zeros(c_z)},
+      "tri_out": trimul(), "tri_in": trimul(),
+      "tri_attn_start": attn(c_z, heads_pair, bias_from=c_z), "tri_attn_end": attn(c_z, heads_pair, bias_from=c_z),
+      "pair_transition": trans(c_z), "d_head": d_head,
+  }
+
+
+def cuda_kernels():
+  """The production namespace: every op is a kernel of libcfk_b200 except the two transitions' GEMMs, which this
+  build leaves to the library GEMM (the fused LN-MLP transition is the next op on the list)."""
+  from colabfold_kernels import ops
+
+  def transition(x, ln, w1, b1, w2, b2):
+    y = ops.layer_norm(x, ln[0], ln[1])
+    h = torch.relu(torch.addmm(b1, y, w1))
+    return torch.addmm(b2, h, w2) + x
+
+  return types.SimpleNamespace(
+      ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,
+      opm_projection=ops.opm_projection, outer_product_mean=ops.outer_product_mean,
+      ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, trimul_epilogue=ops.trimul_epilogue,
+      transition=transition)
+
+
+# ------------------------------------------------------------------------------------------ building blocks
+def head_bias(K, x, prm):
+  """Per-head attention bias from a (shard of the) pair representation x [a, b, c] -> [h, a, b]."""
+  a, b, c = x.shape
+  _, bias = K.ln_projection(x.reshape(a * b, c), prm["bias_ln"][0], prm["bias_ln"][1], None, prm["wb"])
+  return bias.reshape(-1, a, b)
+
+
+def attend(K, x, prm, bias, kmask, column, d_head):
+  """Gated self-attention along axis 1 (rows) or axis 0 (columns) of x [X, Y, c] with residual update."""
+  X, Y, c = x.shape
+  h = prm["heads"]
+  p, _ = K.ln_projection(x.reshape(X * Y, c), prm["ln"][0], prm["ln"][1], prm["w"], None)
+  o = K.packed_attention(p.reshape(X, Y, 4, h, d_head), bias, kmask, prm["gate_bias"], d_head ** -0.5, column=column)
+  return K.output_projection(o.reshape(X * Y, h * d_head), prm["wo"], prm["bo"], x.reshape(X * Y, c)).reshape(X, Y, c)
+
+
+def triangle_update(K, pair_rows, x_cm, prm):
+  """Center LayerNorm, output projection, sigmoid gate from the re-normed input, residual add (one kernel)."""
+  a, b, c = pair_rows.shape
+  out = K.trimul_epilogue(x_cm.reshape(x_cm.shape[0], a * b), pair_rows.reshape(a * b, c), prm["center_ln"][0],
+                          prm["center_ln"][1], prm["wo"], prm["bo"], prm["wgo"], prm["bgo"], in_scale=prm["ln"][0],
+                          in_offset=prm["ln"][1], add_input=True)
+  return out.reshape(a, b, c)
+
+
+def transition(K, x, prm):
+  shape = x.shape
+  return K.transition(x.reshape(-1, shape[-1]), prm["ln"], prm["w1"], prm["b1"], prm["w2"], prm["b2"]).reshape(shape)
+
+
+def block(K, msa, pair, msa_mask, pair_mask, params):
+  """One Evoformer block on one device.  msa [s, r, c_m], pair [r, r, c_z], msa_mask [s, r], pair_mask [r, r] (0/1)."""
+  d = params["d_head"]
+  mm, pm = msa_mask > 0, pair_mask > 0
+  msa = attend(K, msa, params["row_attn"], head_bias(K, pair, params["row_attn"]), mm, False, d)
+  msa = attend(K, msa, params["col_attn"], None, mm.t().contiguous(), True, d)
+  msa = transition(K, msa, params["msa_transition"])
+  o = params["opm"]
+  left, right = K.opm_projection(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
+  pair = K.outer_product_mean(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair)
+  for name, incoming in (("tri_out", False), ("tri_in", True)):
+    t = params[name]
+    l, r = K.ln_gated_dual_proj(pair, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], pair_mask.to(pair.dtype),
+                                transpose=incoming)
+    pair = triangle_update(K, pair, K.contract(r, l) if incoming else K.contract(l, r), t)
+  pair = attend(K, pair, params["tri_attn_start"], head_bias(K, pair, params["tri_attn_start"]), pm, False, d)
+  bias_end = head_bias(K, pair, params["tri_attn_end"]).transpose(1, 2).contiguous()
+  pair = attend(K, pair, params["tri_attn_end"], bias_end, pm.t().contiguous(), True, d)
+  pair = transition(K, pair, params["pair_transition"])
+  return msa, pair
+
+
+# ------------------------------------------------------------------------------------------ sharded over P ranks
+class ShardedBlock:
+  """The same block with the MSA sharded over sequences and the pair over rows, one rank per GPU.
+
+  Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
+  replicated.  s and r must be divisible by the world size."""
+
+  def __init__(self, K, params, group=None):
+    import torch.distributed as dist
+    self.K, self.params, self.dist, self.group = K, params, dist, group
+    self.P = dist.get_world_size(group)
+    self.rank = dist.get_rank(group)
+
+  # dim 0 sharded -> dim 1 sharded: [n0/P, n1, c] -> [n0, n1/P, c]
+  def rows_to_cols(self, x):
+    P = self.P
+    n0, n1, c = x.shape
+    send = x.reshape(n0, P, n1 // P, c).permute(1, 0, 2, 3).contiguous()
+    recv = torch.empty_like(send)
+    self.dist.all_to_all_single(recv, send, group=self.group)
+    return recv.reshape(P * n0, n1 // P, c)
+
+  # dim 1 sharded -> dim 0 sharded: [n0, n1/P, c] -> [n0/P, n1, c]
+  def cols_to_rows(self, x):
+    P = self.P
+    n0, n1, c = x.shape
+    send = x.reshape(P, n0 // P, n1, c).contiguous()
+    recv = torch.empty_like(send)
+    self.dist.all_to_all_single(recv, send, group=self.group)
+    return recv.permute(1, 0, 2, 3).reshape(n0 // P, P * n1, c)
+
+  def gather(self, x, dim):
+    x = x.contiguous()
+    out = torch.empty((self.P * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    self.dist.all_gather_into_tensor(out, x, group=self.group)
+    return out if dim == 0 else torch.cat(list(out.view((self.P,) + tuple(x.shape)).unbind(0)), dim=dim)
+
+  def shard(self, n):
+    step = n // self.P
+    return slice(self.rank * step, (self.rank + 1) * step)
+
+  def __call__(self, msa_s, pair_r, msa_mask, pair_mask):
+    K, prm, d = self.K, self.params, self.params["d_head"]
+    s, r = msa_mask.shape
+    ss, rs = self.shard(s), self.shard(r)
+    mm, pm = msa_mask > 0, pair_mask > 0
+    # 1 MSA row attention: sequences are independent; the pair bias is assembled from every rank's rows
+    bias = self.gather(head_bias(K, pair_r, prm["row_attn"]), 1)
+    msa_s = attend(K, msa_s, prm["row_attn"], bias, mm[ss].contiguous(), False, d)
+    # 2-3 column attention and transition on the residue-sharded MSA
+    msa_c = self.rows_to_cols(msa_s)
+    msa_c = attend(K, msa_c, prm["col_attn"], None, mm.t()[rs].contiguous(), True, d)
+    msa_c = transition(K, msa_c, prm["msa_transition"])
+    # 4 outer product mean: local left projection against everyone's right projection -> local pair rows
+    o = prm["opm"]
+    mloc = msa_mask[:, rs].contiguous()
+    left, right = K.opm_projection(msa_c, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], mloc.to(msa_c.dtype))
+    pair_r = K.outer_product_mean(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r)
+    msa_s = self.cols_to_rows(msa_c)
+    # 5 triangle multiplication, outgoing edges: local rows of the left operand, all rows of the right
+    t = prm["tri_out"]
+    l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
+                                 pair_mask[rs].contiguous().to(pair_r.dtype))
+    pair_r = triangle_update(K, pair_r, K.contract(l, self.gather(rr, 1)), t)
+    # 6 incoming edges: operands come from the column-sharded pair, read transposed
+    t = prm["tri_in"]
+    pair_c = self.rows_to_cols(pair_r)
+    l, rr = K.ln_gated_dual_proj(pair_c, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
+                                 pair_mask[:, rs].contiguous().to(pair_r.dtype), transpose=True)
+    pair_r = triangle_update(K, pair_r, K.contract(rr, self.gather(l, 1)), t)
+    # 7 triangle attention, starting node
+    bias = self.gather(head_bias(K, pair_r, prm["tri_attn_start"]), 1)
+    pair_r = attend(K, pair_r, prm["tri_attn_start"], bias, pm[rs].contiguous(), False, d)
+    # 8 ending node on the column-sharded pair
+    pair_c = self.rows_to_cols(pair_r)
+    bias_end = self.gather(head_bias(K, pair_c, prm["tri_attn_end"]), 2).transpose(1, 2).contiguous()
+    pair_c = attend(K, pair_c, prm["tri_attn_end"], bias_end, pm.t()[rs].contiguous(), True, d)
+    pair_r = self.cols_to_rows(pair_c)
+    # 9 pair transition
+    pair_r = transition(K, pair_r, prm["pair_transition"])
+    return msa_s, pair_r

@@ -58,3 +58,154 @@ def layer_norm(global_config, dtype):
     return None
   from colabfold_kernels import grads
   return grads.layer_norm
+
+
+def _half_ok(global_config, dtype):
+  """The forward-only fused kernels run in bfloat16 (fused_ops.py:67-72 `_pallas_half`; float16 has no kernels here)."""
+  return _enabled(global_config) and _norm_dtype(dtype) == torch.bfloat16
+
+
+def _k_ok(k):
+  return k in (64, 128, 256)
+
+
+def fp8_attention(global_config, key_dim):
+  """e4m3 k/v slots for packed attention are not built for this backend (fused_ops.py:75-80)."""
+  return False
+
+
+def fp8_attention_slots(global_config, dtype, key_dim, seq_len):
+  return None
+
+
+def half_attention(global_config):
+  """The f16 softmax is an Ampere/Hopper tuning (fused_ops.py:142-149): off."""
+  return False
+
+
+def packed_attention(global_config, dtype, key_dim, value_dim):
+  """-> f(p, bias, kmask, gate_bias, *, sm_scale, column) or None; p is the packed [X, Y, G, H, D] projection
+  (fused_ops.py:152-178).  global_config.trim_padding selects the trim semantics."""
+  if attention(global_config, dtype, key_dim, value_dim) is None or key_dim != value_dim:
+    return None
+  from colabfold_kernels import grads
+  return functools.partial(grads.packed_attention, trim=bool(global_config.get("trim_padding", False)))
+
+
+def gated_dual_proj(global_config, dtype, activation=None):
+  """-> f(x, wp, bp, wg, bg, mask, *, split, channel_major) or None; activation None/'sigmoid' or 'swish'
+  (fused_ops.py:393-413)."""
+  if not _half_ok(global_config, dtype):
+    return None
+  name = getattr(activation, "__name__", activation)
+  act = {None: 0, "sigmoid": 0, "swish": 1, "silu": 1}.get(name)
+  if act is None:
+    return None
+  from colabfold_kernels import grads
+
+  def call(x, wp, bp, wg, bg, mask, *, split=False, channel_major=False):
+    if not _k_ok(x.shape[-1]):
+      raise ValueError("gated_dual_proj: contracted width must be 64, 128 or 256")
+    return grads.gated_dual_proj(x, wp, bp, wg, bg, mask, split=split, channel_major=channel_major, activation=act)
+  return call
+
+
+def ln_gated_dual_proj(global_config, dtype, num_channel, num_intermediate):
+  """-> f(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, *, eps, transpose) -> (left, right) channel major, or None
+  (fused_ops.py:238-259)."""
+  if not _half_ok(global_config, dtype) or not _k_ok(num_channel) or num_intermediate % 64 != 0:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.ln_gated_dual_proj, reference.ref_ln_gdp, nondiff=("eps", "transpose", "pad"))
+
+
+def fp8_contraction(global_config, dtype, num_channel, num_intermediate, num_res):
+  """-> (projection, contract) or None: the projection writing e4m3 halves padded to 16 and their contraction
+  (fused_ops.py:262-275)."""
+  if not global_config.get("fp8", False) or num_res % 8 != 0:
+    return None
+  if ln_gated_dual_proj(global_config, dtype, num_channel, num_intermediate) is None:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  proj = grads.differentiable_via(functools.partial(ops.ln_gated_dual_proj, fp8=True, pad=16),
+                                  functools.partial(reference.ref_ln_gdp, pad=16), nondiff=("eps", "transpose"))
+  return proj, grads.differentiable_via(ops.contract, reference.ref_contract)
+
+
+def contraction(global_config, dtype):
+  """-> f(a, b) -> [C, I, J] bf16 for a [C, I, K], b [C, J, K], or None.  The reference leaves the bf16 contraction
+  to XLA's batched GEMM (tri_mul.py:6-7); here it is a kernel of the library."""
+  if not _half_ok(global_config, dtype):
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.contract, reference.ref_contract)
+
+
+def trimul_epilogue(global_config, dtype):
+  """-> f(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, *, eps) or None (fused_ops.py:212-218)."""
+  if not _half_ok(global_config, dtype):
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.trimul_epilogue, reference.ref_trimul_epilogue, nondiff=("eps",))
+
+
+def trimul_epilogue_ln(global_config, dtype):
+  """-> f(x_cm, x, in_scale, in_offset, ln_scale, ln_offset, wo, bo, wg, bg, *, eps, add_input) or None
+  (fused_ops.py:221-235)."""
+  if not _half_ok(global_config, dtype):
+    return None
+  from colabfold_kernels import grads, ops, reference
+
+  def fwd(x_cm, x, in_scale, in_offset, ln_scale, ln_offset, wo, bo, wg, bg, keep=None, *, eps=1e-5, add_input=False):
+    return ops.trimul_epilogue(x_cm, x, ln_scale, ln_offset, wo, bo, wg, bg, in_scale=in_scale, in_offset=in_offset,
+                               eps=eps, add_input=add_input)
+  return grads.differentiable_via(fwd, reference.ref_trimul_epilogue_ln, nondiff=("eps", "add_input"))
+
+
+def ln_projection(global_config, dtype, num_channel, num_output=None):
+  """-> f(x, ln_scale, ln_offset, w, wb, *, eps) -> (p, bias) or None (fused_ops.py:278-304)."""
+  if not _half_ok(global_config, dtype) or not _k_ok(num_channel):
+    return None
+  if num_output is not None and num_output % 64 != 0:
+    return None
+  from colabfold_kernels import grads, ops, reference
+
+  def fwd(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5):
+    return ops.ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps)
+  return grads.differentiable_via(fwd, reference.ref_ln_projection, nondiff=("eps",))
+
+
+def output_projection(global_config, dtype, num_input, num_output):
+  """-> f(o, w, b, residual=None) or None (fused_ops.py:307-323)."""
+  if not _half_ok(global_config, dtype) or not _k_ok(num_input) or num_output % 8 != 0:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.output_projection, reference.ref_output_projection)
+
+
+def opm_projection(global_config, dtype, num_channel, num_outer):
+  """-> f(x, ln_scale, ln_offset, lw, lb, rw, rb, mask, *, eps) -> (left_act, right_act) or None (fused_ops.py:364-372)."""
+  if not _half_ok(global_config, dtype) or not _k_ok(num_channel) or num_outer % 8 != 0 or num_outer > 128:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.opm_projection, reference.ref_opm_projection, nondiff=("eps",))
+
+
+def opm_update(global_config, dtype, num_inner, num_output):
+  """The shallow-MSA pair update (fused_ops.py:326-342) has no kernel in this build: the caller runs its own path."""
+  return None
+
+
+def opm_outer(global_config, dtype, rows, num_inner, d, num_output):
+  """The 16-row outer product (fused_ops.py:345-361) has no kernel in this build: the caller runs its own path."""
+  return None
+
+
+def transition(global_config, dtype, num_channel, num_intermediate):
+  """The fused LN-MLP transition (fused_ops.py:181-198) has no kernel in this build yet: the caller runs its own path."""
+  return None
+
+
+def glu_transition(global_config, dtype, num_channel, num_intermediate):
+  """AF3's swish-GLU transition (fused_ops.py:201-209) is outside the Evoformer path: None."""
+  return None

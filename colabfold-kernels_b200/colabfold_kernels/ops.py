@@ -259,3 +259,32 @@ def opm_projection(x, ln_scale, ln_offset, lw, lb, rw, rb, mask, eps=1e-5):
               _ptr(_c(lb.to(dt))), _ptr(_c(rw.to(dt))), _ptr(_c(rb.to(dt))), _ptr(_c(mask.to(dt))), _ptr(left),
               _ptr(right), m, c, k, float(eps), _stream())
   return left, right
+
+
+def opm_finish(x, bias, norm, residual=None, eps=1e-3, out=None):
+  """(x + bias) / (eps + norm[..., None]) + residual; x [..., f] bf16, norm [...] fp32."""
+  x = _c(x)
+  f = x.shape[-1]
+  m = x.numel() // f
+  if out is None:
+    out = torch.empty_like(x)
+  res = None if residual is None else _c(residual.to(x.dtype))
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_opm_finish", _ptr(x), _ptr(_c(bias.to(x.dtype))), _ptr(_f32(norm)), _ptr(res), _ptr(out), m, f,
+              float(eps), _stream())
+  return out
+
+
+def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+  """Deep-MSA outer product mean from the masked projections left [s, ri, c], right [s, rj, c]: two tensor-core GEMMs
+  (the outer product over the MSA depth, rounded to bf16 as the reference's opm_outer does, opm.py:124-134; then the
+  output weights w [c*c, f]) and the normalising tail -> [ri, rj, f].  ri < rj when the pair is row-sharded."""
+  s, ri, c = left.shape
+  rj, e = right.shape[1], right.shape[2]
+  a = left.permute(1, 2, 0).reshape(1, ri * c, s).contiguous()       # [(i,c), s]
+  b = right.permute(1, 2, 0).reshape(1, rj * e, s).contiguous()      # [(j,e), s]
+  outer = contract(a, b).view(ri, c, rj, e).permute(0, 2, 1, 3).reshape(1, ri * rj, c * e).contiguous()
+  wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
+  x = contract(outer, wt).view(ri, rj, w.shape[1])
+  norm = mask_left.float().t() @ mask_right.float()
+  return opm_finish(x, bias, norm, residual, eps)

@@ -161,6 +161,12 @@ CFK_API int cfk_opm_projection(const void* x, const float* ln_scale, const float
                                const void* lb, const void* rw, const void* rb, const void* mask, void* left,
                                void* right, int64_t m, int c, int k, float eps, void* stream);
 
+/* Outer-product-mean tail: out[m,f] = (x[m,f] + bias[f]) / (eps + norm[m]) + residual[m,f] (residual may be NULL,
+ * out may alias it); x, bias, residual, out bf16, norm fp32.  The pair update of opm_update, opm.py:69-88,116-119,
+ * applied after the two GEMMs of the deep-MSA outer product (cfk_contract). */
+CFK_API int cfk_opm_finish(const void* x, const void* bias, const float* norm, const void* residual, void* out,
+                           int64_t m, int f, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

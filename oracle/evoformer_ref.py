@@ -1,0 +1,49 @@
+"""An ops namespace for colabfold_kernels.evoformer built on the CPU oracle (test infrastructure only).
+
+The block wiring is not in the reference (it lives in ColabFold/AlphaFold): parity of the composition is
+unpinned; each op it calls is the pinned restatement from reference_math."""
+import types
+
+import torch
+
+from oracle import reference_math as R
+
+
+def oracle_kernels(dtype=torch.float32):
+  def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5):
+    return R.ref_ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps, dtype=dtype)
+
+  def packed_attention(p, bias, kmask, gate_bias, sm_scale, column=False):
+    return R.ref_packed_attention(p, bias, kmask, gate_bias, sm_scale=sm_scale, column=column, dtype=dtype)
+
+  def output_projection(o, w, b, residual=None):
+    return R.ref_output_projection(o, w, b, residual, dtype=dtype)
+
+  def opm_projection(x, s, o, lw, lb, rw, rb, mask, eps=1e-5):
+    return R.ref_opm_projection(x, s, o, lw, lb, rw, rb, mask, eps=eps, dtype=dtype)
+
+  def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+    out = R.ref_opm_outer(left, right, w, dtype) + bias.to(dtype)
+    out = out / (eps + mask_left.to(dtype).T @ mask_right.to(dtype))[..., None]
+    return out if residual is None else out + residual.to(dtype)
+
+  def ln_gated_dual_proj(x, s, o, wp, bp, wg, bg, mask, eps=1e-5, transpose=False, pad=1):
+    return R.ref_ln_gdp(x, s, o, wp, bp, wg, bg, mask, eps=eps, transpose=transpose, pad=pad, dtype=dtype)
+
+  def contract(a, b):
+    return R.ref_contract(a, b, dtype)
+
+  def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, in_scale=None, in_offset=None,
+                      eps=1e-5, add_input=False):
+    if in_scale is None:
+      return R.ref_trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual, eps=eps, dtype=dtype)
+    return R.ref_trimul_epilogue_ln(x_cm, act, in_scale, in_offset, ln_scale, ln_offset, wo, bo, wg, bg, eps=eps,
+                                    add_input=add_input, dtype=dtype)
+
+  def transition(x, ln, w1, b1, w2, b2):
+    return R.ref_transition(x, ln[0], ln[1], w1, b1, w2, b2, add_input=True, dtype=dtype)
+
+  return types.SimpleNamespace(ln_projection=ln_projection, packed_attention=packed_attention,
+                               output_projection=output_projection, opm_projection=opm_projection,
+                               outer_product_mean=outer_product_mean, ln_gated_dual_proj=ln_gated_dual_proj,
+                               contract=contract, trimul_epilogue=trimul_epilogue, transition=transition)
