@@ -13,6 +13,7 @@ int run_chunks(RowGemmParams prm, int total_chunks, const void* w0, const void* 
                cudaStream_t st) {
   const int nsrc = prm.src[1].x != nullptr ? 2 : 1;
   const int k0 = prm.src[0].k, k1 = nsrc == 2 ? prm.src[1].k : k0;
+  prm.chunks = 1;
   CUtensorMap tw0, tw1;
   int rc = make_weight_map(&tw0, w0, slots, k0, n_cols);
   if (rc != CFK_OK) return rc;
@@ -22,10 +23,7 @@ int run_chunks(RowGemmParams prm, int total_chunks, const void* w0, const void* 
   } else {
     tw1 = tw0;
   }
-  const int a_bytes = 2 * (k0 / 64) * 16384 + (nsrc == 2 ? 2 * (k1 / 64) * 16384 : 0);
-  const int w_per_chunk = (prm.n_chunk / 64) * 128 * (k0 + (prm.dual ? k1 : 0));
-  const int budget = 232448 - 1024 - 256 - a_bytes - 8 * (k0 + k1);
-  int fit = budget / w_per_chunk;
+  int fit = rowgemm_chunks_that_fit(prm);
   if (fit < 1) return CFK_ERR_UNSUPPORTED;
   prm.status = device_status_word();
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
@@ -65,7 +63,7 @@ extern "C" int cfk_gated_dual_proj(const void* x, const void* wp, const void* bp
   prm.chunks_per_array = cpa;
   prm.chunks_per_slot = split ? 2 * cpa : cpa;
   prm.bias_slot_stride = 0;
-  prm.bias[0] = bp; prm.bias[1] = bg;
+  prm.bias[0] = bp; prm.bias[1] = bg; prm.bias_len = p;
   prm.rowmask = mask; prm.rowmask_dtype = CFK_BF16;
   prm.out[0] = out0; prm.out[1] = out1;
   prm.ldo = width; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
@@ -97,7 +95,7 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   if (ci % prm.n_chunk != 0) return CFK_ERR_UNSUPPORTED;
   const int cpa = ci / prm.n_chunk;
   prm.chunks_per_array = cpa; prm.chunks_per_slot = 2 * cpa; prm.bias_slot_stride = 0;
-  prm.bias[0] = bp; prm.bias[1] = bg;
+  prm.bias[0] = bp; prm.bias[1] = bg; prm.bias_len = p;
   prm.rowmask = mask; prm.rowmask_dtype = CFK_BF16;
   prm.out[0] = left; prm.out[1] = right;
   prm.ldo = ci; prm.out_dtype = fp8 ? CFK_E4M3 : CFK_BF16; prm.out_scale = 1.f;
@@ -123,7 +121,7 @@ extern "C" int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void*
   prm.n_chunk = o >= 128 ? 128 : 64;
   const int cpa = (o + prm.n_chunk - 1) / prm.n_chunk;
   prm.chunks_per_array = cpa; prm.chunks_per_slot = cpa; prm.bias_slot_stride = 0;
-  prm.bias[0] = bo; prm.bias[1] = bg;
+  prm.bias[0] = bo; prm.bias[1] = bg; prm.bias_len = o;
   prm.out[0] = out; prm.ldo = o; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f; prm.n_valid = o;
   prm.residual = residual; prm.add_source1 = add_input;
   // the two weights have different K (c and ca): separate maps inside run_chunks use src[0].k and src[1].k
@@ -177,7 +175,7 @@ extern "C" int cfk_output_projection(const void* o, const void* w, const void* b
   prm.n_chunk = c >= 128 ? 128 : 64;
   const int cps = (c + prm.n_chunk - 1) / prm.n_chunk;
   prm.chunks_per_slot = cps; prm.chunks_per_array = cps;
-  prm.bias[0] = b;
+  prm.bias[0] = b; prm.bias_len = c;
   prm.out[0] = out; prm.ldo = c; prm.n_valid = c; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
   prm.residual = residual;
   return run_chunks(prm, cps, w, nullptr, 1, c, static_cast<cudaStream_t>(stream));
@@ -196,7 +194,7 @@ extern "C" int cfk_opm_projection(const void* x, const float* ln_scale, const fl
   prm.mode = kModeLinear; prm.dual = 1;  // two independent outputs from one normed tile
   prm.n_chunk = k > 64 ? 128 : 64;
   prm.chunks_per_slot = 1; prm.chunks_per_array = 1;
-  prm.bias[0] = lb; prm.bias[1] = rb;
+  prm.bias[0] = lb; prm.bias[1] = rb; prm.bias_len = k;
   prm.rowmask = mask; prm.rowmask_dtype = CFK_BF16;
   prm.out[0] = left; prm.out[1] = right; prm.ldo = k; prm.n_valid = k; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
   return run_chunks(prm, 1, lw, rw, 1, k, static_cast<cudaStream_t>(stream));

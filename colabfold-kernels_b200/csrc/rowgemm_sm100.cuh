@@ -3,9 +3,11 @@
 // packed projection, output projection, outer-product-mean projection).
 //
 // A persistent CTA walks 128-row tiles.  Per tile:
-//   prologue warps (4)  one thread per row: load the row (row-major source, optionally through a pair transpose,
-//                       or a channel-major source), LayerNorm it in fp32 registers, round to bf16 and write it as a
-//                       128-byte-swizzled K-major UMMA operand into one of two shared-memory stages
+//   producer thread     TMA loads of the tile of every source into a ring of shared-memory stages: a row-major
+//                       source (optionally through a pair transpose) lands directly as the 128-byte-swizzled
+//                       K-major UMMA operand, a channel-major source as [K][128 rows]
+//   prologue warps (4)  one thread per row: LayerNorm the landed row in fp32 and rewrite it in place as bf16
+//                       (a channel-major tile is transposed into the operand layout on the way)
 //   MMA issuer          for every 128-column chunk of the output: acc0 = A0 W0 (and acc1 = A1 W1) with the
 //                       weights resident in shared memory in their natural [K, N] layout (MN-major B operand)
 //   epilogue warps (4)  TMEM -> registers -> bias / activation / mask / residual -> bf16 (or e4m3) -> global
@@ -45,6 +47,7 @@ struct RowGemmParams {
   int chunks_per_slot;              // global chunk c -> weight slot c / chunks_per_slot, column (c % chunks_per_slot) * n_chunk
   int bias_slot_stride;             // bias index = slot * bias_slot_stride + column
   const void* bias[2];              // bf16 [N] per accumulator or nullptr (indexed by absolute output column)
+  int bias_len;                     // entries of each bias vector
   const void* rowmask;              // [rows] in src[0] order (bf16 or fp32 by rowmask_dtype) or nullptr
   int rowmask_dtype;
   // row-major output: out[i][row * ldo + col0[i] + chunk columns]; chunk c of accumulator i lands in array
@@ -61,6 +64,7 @@ struct RowGemmParams {
   int* status;
 };
 
+int rowgemm_chunks_that_fit(const RowGemmParams& prm);  // chunks whose weights fit beside two pipeline stages
 int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st);
 int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
 
