@@ -106,12 +106,51 @@ def cpu_arm(steps, warmup, sample_b=2):
                     f"median of {len(times)}", "ms_per_sample": sec * 1e3}
 
 
+def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024):
+  """Second metric: one Evoformer block (inference wiring of the fused ops) at N_seq=512, N_res=1024, device-timed,
+  max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed)."""
+  import torch
+  import torch.distributed as dist
+  from colabfold_kernels import evoformer
+  bf = torch.bfloat16
+  g = torch.Generator().manual_seed(5)
+  msa = torch.randn(n_seq, n_res, 256, generator=g).to(bf)
+  pair = torch.randn(n_res, n_res, 128, generator=g).to(bf)
+  msa_mask = (torch.rand(n_seq, n_res, generator=g) < 0.95).float().to(dev)
+  pair_mask = (torch.rand(n_res, n_res, generator=g) < 0.95).float().to(dev)
+  params = evoformer.init_params(device=dev)
+  K = evoformer.cuda_kernels()
+  if world > 1:
+    blk = evoformer.ShardedBlock(K, params)
+    msa_l, pair_l = msa[blk.shard(n_seq)].to(dev), pair[blk.shard(n_res)].to(dev)
+    run = lambda: blk(msa_l, pair_l, msa_mask, pair_mask)
+  else:
+    msa_l, pair_l = msa.to(dev), pair.to(dev)
+    run = lambda: evoformer.block(K, msa_l, pair_l, msa_mask, pair_mask, params)
+  for _ in range(2):
+    run()
+  if world > 1:
+    dist.barrier()
+  torch.cuda.synchronize()
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  e0.record()
+  for _ in range(iters):
+    run()
+  e1.record()
+  torch.cuda.synchronize()
+  ms = torch.tensor([e0.elapsed_time(e1) / iters], device=dev)
+  if world > 1:
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+  return float(ms)
+
+
 def main():
   ap = argparse.ArgumentParser()
   ap.add_argument("--gpus", type=int, default=1)
   ap.add_argument("--steps", type=int, default=5)
   ap.add_argument("--warmup", type=int, default=3)
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+  ap.add_argument("--block", type=int, default=1, help="also time one Evoformer block (0 to skip)")
   args = ap.parse_args()
   rank = int(os.environ.get("RANK", "0"))
   world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -222,6 +261,8 @@ def main():
   e2e_ms = torch.tensor([t0.elapsed_time(t1) / n_e2e], device=dev)
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+  block_ms = evoformer_block_ms(world, rank, dev) if args.block else None
+  status = ops.device_status()
   if rank == 0:
     sampler.stop_flag.set()
     sampler.join(timeout=2)
@@ -240,7 +281,11 @@ def main():
         "config": {"workload": WORKLOAD, "global_batch": B * world, "parallelism": f"batch-sharded x{world}, no collective",
                    "l2": "inputs (1.1 GB per rank) exceed the 126 MB L2; no flush between steps",
                    "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
-                   "device_status": status},
+                   "device_status": status,
+                   "evoformer_block": None if block_ms is None else {
+                       "ms": block_ms, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
+                       "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
+                       "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms)},
         "gpu_launches": int(launches),
