@@ -3,6 +3,7 @@
 // allows), the two row statistics are warp-shuffle reductions in fp32, and several rows per warp
 // are in flight so the loads of one row overlap the arithmetic of the previous.
 // Math: src/colabfold_kernels/tri_mul.py:463-485,515-520; backward: grads.py:25-39.
+#include <mutex>
 #include "cfk_common.cuh"
 
 namespace cfk {
@@ -300,6 +301,71 @@ extern "C" int cfk_layer_norm_bwd(const void* x, const float* scale, const void*
   else
     return CFK_ERR_DTYPE;
   int rc = check_launch();
+  if (rc != CFK_OK) return rc;
+  ln_bwd_fold_kernel<<<(2 * c + 127) / 128, 128, 0, st>>>(partial, dscale, doffset, blocks, c);
+  return check_launch();
+}
+
+// ---- LayerNorm backward with built-in scratch -----------------------------------------------------------
+// The same two kernels as cfk_layer_norm_bwd, with the per-block partial sums in a fixed array that is part of
+// this module's device image instead of a caller workspace: the entry allocates nothing, on the device or through
+// any library.
+namespace cfk {
+namespace {
+
+constexpr int kStaticMaxC = 256;       // widest row the built-in scratch takes
+constexpr int kStaticMaxBlocks = 512;  // most blocks it takes (the launch uses 2 per SM)
+static __device__ __align__(256) float g_ln_bwd_partial[static_cast<size_t>(kStaticMaxBlocks) * 2 * kStaticMaxC];  // 1 MiB
+
+constexpr int kStaticMaxDevices = 64;
+float* g_ln_bwd_partial_addr[kStaticMaxDevices] = {};  // device address of the array, per device
+std::mutex g_ln_bwd_partial_mutex;
+
+// Set-up, once per device and with that device current: the array's name is not a device address in host code,
+// the runtime has to be asked for it.  This also makes the runtime load this module's image on the device.
+int static_partial(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) return CFK_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_ln_bwd_partial_mutex);
+  if (g_ln_bwd_partial_addr[dev] == nullptr) {
+    float* ptr = nullptr;
+    if (cudaGetSymbolAddress((void**)&ptr, g_ln_bwd_partial) != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return CFK_ERR_LAUNCH;
+    }
+    g_ln_bwd_partial_addr[dev] = ptr;
+  }
+  *out = g_ln_bwd_partial_addr[dev];
+  return CFK_OK;
+}
+
+}  // namespace
+}  // namespace cfk
+
+extern "C" int cfk_layer_norm_bwd_static(const void* x, const float* scale, const void* dy, void* dx, float* dscale,
+                                         float* doffset, int64_t m, int c, int dtype, float eps, void* stream) {
+  using namespace cfk;
+  if (x == nullptr || scale == nullptr || dy == nullptr || dx == nullptr || dscale == nullptr || doffset == nullptr)
+    return CFK_ERR_NULL;
+  if (m <= 0 || c <= 0) return CFK_ERR_SHAPE;
+  if (dtype != CFK_BF16 && dtype != CFK_F32) return CFK_ERR_DTYPE;
+  const int blocks = sm_count() * kBwdBlocksPerSm;
+  if (c > kStaticMaxC || blocks > kStaticMaxBlocks) return CFK_ERR_WORKSPACE;  // beyond the built-in scratch
+  float* partial = nullptr;
+  int rc = static_partial(&partial);
+  if (rc != CFK_OK) return rc;
+  // Nothing has to start at zero: every block overwrites its whole row of 2*c partial sums before the fold reads it.
+  auto st = static_cast<cudaStream_t>(stream);
+  const size_t smem = kWarpsPerBlock * 2 * static_cast<size_t>(c) * sizeof(float);
+  if (dtype == CFK_BF16)
+    ln_bwd_kernel<__nv_bfloat16><<<blocks, kWarpsPerBlock * 32, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), scale, static_cast<const __nv_bfloat16*>(dy),
+        static_cast<__nv_bfloat16*>(dx), partial, m, c, eps);
+  else
+    ln_bwd_kernel<float><<<blocks, kWarpsPerBlock * 32, smem, st>>>(static_cast<const float*>(x), scale,
+                                                                    static_cast<const float*>(dy),
+                                                                    static_cast<float*>(dx), partial, m, c, eps);
+  rc = check_launch();
   if (rc != CFK_OK) return rc;
   ln_bwd_fold_kernel<<<(2 * c + 127) / 128, 128, 0, st>>>(partial, dscale, doffset, blocks, c);
   return check_launch();

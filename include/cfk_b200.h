@@ -65,6 +65,23 @@ CFK_API size_t cfk_layer_norm_bwd_workspace_bytes(int64_t m, int c);
 CFK_API int cfk_layer_norm_bwd(const void* x, const float* scale, const void* dy, void* dx, float* dscale, float* doffset,
                        int64_t m, int c, int dtype, float eps, void* workspace, size_t workspace_bytes, void* stream);
 
+/* cfk_layer_norm_bwd without a workspace argument and without any allocation: the per-block partial sums
+ * live in a fixed 1 MiB array inside the library's device image.  It has no counterpart in the reference
+ * (whose handlers get all scratch from XLA).  For callers that hold no allocator at the call site and may
+ * not call one: a handler running inside a pre-planned buffer assignment, or a replay-only serving loop
+ * whose memory pool is frozen after start-up.
+ *   - Limits: c <= 256 and at most 512 launch blocks (two per SM); beyond either the call does nothing
+ *     and returns CFK_ERR_WORKSPACE.
+ *   - The first call on each device performs set-up (it asks the runtime for the array's device address,
+ *     which also loads the module there): make it once, with that device current, before any stream
+ *     capture is begun.  Later calls only launch.
+ *   - Nothing needs clearing between calls: the kernels overwrite every partial sum they later read.
+ *   - The array is shared by all callers of this entry on a device: two calls that overlap in time
+ *     (different streams or threads) race on it.  Issue them on one stream, or order them.
+ * Results are bit-identical to cfk_layer_norm_bwd. */
+CFK_API int cfk_layer_norm_bwd_static(const void* x, const float* scale, const void* dy, void* dx, float* dscale,
+                              float* doffset, int64_t m, int c, int dtype, float eps, void* stream);
+
 /* ---- Bias-fused attention ---------------------------------------------------------------------------
  * out = softmax_k(scale * q.k + bias[h,q,k], masked keys -> finite floor) . v, per (batch n, head h).
  * q [n,h,sq,d] ('heads') or [n,sq,h,d] (seq_major); k, v likewise with sk; bias [h,sq,sk] in `dtype` or NULL;
