@@ -256,6 +256,20 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     const float scale = p.scale;
     float acc[64];  // dBias of this thread's (query row, 64 keys), summed over the G batch rows of a query block
     int t = 0;
+    // forward statistics of a step's row, fetched one step ahead of their use (rows past Sq get lse = +inf, which
+    // makes p and ds exactly zero)
+    auto fetch_stats = [&](int step, float& lse_out, float& dlt_out) {
+      lse_out = INFINITY;
+      dlt_out = 0.f;
+      const int ii = step / gcount, gg = step - ii * gcount, qq = ii * kBQ + row;
+      if (step < nsteps && qq < p.sq) {
+        const int64_t r = (int64_t(b0 + gg) * p.h + head) * p.sq + qq;
+        lse_out = p.lse[r];
+        dlt_out = prm.delta[r];
+      }
+    };
+    float lse_next, dlt_next;
+    fetch_stats(0, lse_next, dlt_next);
     for (int i = 0; i < ni; ++i) {
       const int q = i * kBQ + row;
 #pragma unroll
@@ -263,14 +277,8 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (prm.has_bias) CFK_BWD_WAIT(bias_full, i & 1, 801)
 #pragma unroll 1
       for (int g = 0; g < gcount; ++g, ++t) {
-        const int b = b0 + g;
-        // forward statistics of this row; rows past Sq get lse = +inf, which makes p and ds exactly zero
-        float lse = INFINITY, dlt = 0.f;
-        if (q < p.sq) {
-          const int64_t r = (int64_t(b) * p.h + head) * p.sq + q;
-          lse = p.lse[r];
-          dlt = prm.delta[r];
-        }
+        const float lse = lse_next, dlt = dlt_next;
+        fetch_stats(t + 1, lse_next, dlt_next);
         CFK_BWD_WAIT(sdp_full, t & 1, 802)
         tc_fence_after();
         const float* madd = mask_all + g * 128 + half * 64;
@@ -304,6 +312,12 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
                 s[c * 8 + 2 * e] = fmaf(s[c * 8 + 2 * e], scale, bf16lo_to_f32(ww[e]));
                 s[c * 8 + 2 * e + 1] = fmaf(s[c * 8 + 2 * e + 1], scale, bf16hi_to_f32(ww[e]));
               }
+            }
+            // the last step of a query block has now read the whole bias tile: release it, so that the next block's
+            // tile loads behind the rest of this step
+            if (hc == 1 && g == gcount - 1) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bias_empty);
             }
           } else {
 #pragma unroll
@@ -341,10 +355,11 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           uint32_t r[16];
           tmem_ld_x16(tmem + lane_addr + kColDq + half * 16, r);
           tmem_wait_ld();
-          float* stg = reinterpret_cast<float*>(smem + kOffDq + ((t - 1) & 1) * kTileDq) + row * D + half * 16;
+          // 128-byte rows, 128-byte swizzle (the reduce's tensor map undoes it): conflict-free 16-byte stores
+          uint8_t* stg = smem + kOffDq + ((t - 1) & 1) * kTileDq;
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<float4*>(stg + c * 4) =
+            *reinterpret_cast<float4*>(stg + swz_off(row, half * 4 + c, 128)) =
                 make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
                             __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
         }
@@ -367,10 +382,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         }
         if (lane == 0) mbar_arrive(pds_full);
       }
-      if (prm.has_bias) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bias_empty);
-      }
       // flush dBias of this query block: the sum over this CTA's batch rows joins the other CTAs' by atomics
       if (prm.bp.dbias != nullptr && ok && q < p.sq) {
         float* dst = prm.bp.dbias + (int64_t(head) * p.sq + q) * p.sk + k0 + half * 64;
@@ -386,10 +397,10 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       uint32_t r[16];
       tmem_ld_x16(tmem + lane_addr + kColDq + half * 16, r);
       tmem_wait_ld();
-      float* stg = reinterpret_cast<float*>(smem + kOffDq + ((nsteps - 1) & 1) * kTileDq) + row * D + half * 16;
+      uint8_t* stg = smem + kOffDq + ((nsteps - 1) & 1) * kTileDq;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<float4*>(stg + c * 4) =
+        *reinterpret_cast<float4*>(stg + swz_off(row, half * 4 + c, 128)) =
             make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
                         __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
       fence_proxy_async();
@@ -507,7 +518,7 @@ int attention_bwd_sm100(const AttnBwdProblem& bp, float* delta, void* workspace,
     uint64_t dims[4] = {uint64_t(D), uint64_t(p.sq), uint64_t(p.h), uint64_t(p.nb)};
     uint64_t strides[3] = {uint64_t(D) * 4, uint64_t(p.sq) * D * 4, uint64_t(p.h) * p.sq * D * 4};
     uint32_t box[4] = {uint32_t(D), kBQ, 1, 1};
-    rc = make_tensor_map(&tdq, dq_acc, CFK_F32, 4, dims, strides, box, 0);
+    rc = make_tensor_map(&tdq, dq_acc, CFK_F32, 4, dims, strides, box, 128);
     if (rc != CFK_OK) return rc;
   }
   BwdParams prm{bp, delta, dq_acc, device_status_word(), p.bias != nullptr};
