@@ -7,8 +7,8 @@
 //                  published P and dS (bf16, shared memory): dV_g += P^T dO, dK_g += dS^T Q, dQ = dS K
 //   softmax warps  8 warps, thread = (query row, half of the 128 keys): p = 2^(s*log2e - lse) from the forward's
 //                  lse, ds = p * (dp - delta); dBias accumulates over the G batch rows in registers and is
-//                  flushed with vector atomics once per query block; the previous step's dQ tile goes
-//                  TMEM -> shared -> fp32 scratch by TMA reduce-add
+//                  flushed with vector atomics during the block's last step; the previous step's dQ tile goes
+//                  TMEM -> shared, from where a reducer warp sends it to the fp32 scratch by TMA reduce-add
 // The bias tile is shared by the G steps of a query block.  dK/dV leave TMEM once, at the end.
 // TMEM columns: S [0,128) dP [128,256) dQ [256,288) | batch row g: dK [288+64g, +32) dV [320+64g, +32).
 // Math: src/colabfold_kernels/tri_flash.py:313-355,380,434-446.
@@ -37,7 +37,7 @@ constexpr int kOffDs = kOffP + kTileBig;
 constexpr int kOffDq = kOffDs + kTileBig;               // [2][kTileDq]
 constexpr int kOffMask = kOffDq + 2 * kTileDq;          // float [G][128]
 constexpr int kOffBar = kOffMask + G * 128 * 4;
-constexpr int kNumBars = G + 2 * kQdoStages + 2 + 2 + 2;
+constexpr int kNumBars = G + 2 * kQdoStages + 2 + 2 + 2 + 4;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmem = kOffTmem + 16 + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -81,6 +81,8 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   uint64_t* sdp_empty = sdp_full + 1;            // ... and have been read into registers
   uint64_t* pds_full = sdp_empty + 1;            // P and dS of a step are in shared memory
   uint64_t* gemm_done = pds_full + 1;            // the three output GEMMs of a step have completed
+  uint64_t* dq_staged = gemm_done + 1;           // [2] a dQ tile is in its staging buffer
+  uint64_t* dq_free = dq_staged + 2;             // [2] the reduce out of a staging buffer has read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,6 +105,10 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     mbar_init(sdp_empty, 8);
     mbar_init(pds_full, 8);
     mbar_init(gemm_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dq_staged[i], 8);
+      mbar_init(&dq_free[i], 1);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -154,6 +160,20 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           tma_load_3d(smem + kOffBias, &tm_bias, bias_full, k0, i * kBQ, head);
           tma_load_3d(smem + kOffBias + kTileBig / 2, &tm_bias, bias_full, k0 + 64, i * kBQ, head);
         }
+      }
+      __syncwarp();
+    } else if (warp == 2) {
+      // ---------------------------------------------------------------- dQ reducer: staging buffer -> fp32 scratch
+      if (lane == 0) {
+        for (int tp = 0; tp < nsteps; ++tp) {
+          if (!mbar_wait_deadline(&dq_staged[tp & 1], (tp >> 1) & 1)) { report_timeout(prm.status, 603); break; }
+          const int ip = tp / gcount, gp = tp - ip * gcount;
+          tma_reduce_add_4d(&tm_dq, smem + kOffDq + (tp & 1) * kTileDq, 0, ip * kBQ, head, b0 + gp);
+          tma_commit_group();
+          tma_wait_group_read<0>();
+          mbar_arrive(&dq_free[tp & 1]);
+        }
+        tma_wait_group<0>();
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -275,6 +295,8 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #pragma unroll
       for (int c = 0; c < 64; ++c) acc[c] = 0.f;
       if (prm.has_bias) CFK_BWD_WAIT(bias_full, i & 1, 801)
+      const bool flush_ok = prm.bp.dbias != nullptr && q < p.sq;
+      float* dbias_row = prm.bp.dbias + (int64_t(head) * p.sq + q) * p.sk + k0 + half * 64;
 #pragma unroll 1
       for (int g = 0; g < gcount; ++g, ++t) {
         const float lse = lse_next, dlt = dlt_next;
@@ -302,6 +324,8 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             __syncwarp();
             if (lane == 0) mbar_arrive(sdp_empty);
           }
+          // packed fp32 pairs from here on: two keys per FMA-pipe instruction
+          const uint64_t scale2 = f2_pack(scale, scale);
           if (prm.has_bias) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -309,8 +333,11 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
               const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                s[c * 8 + 2 * e] = fmaf(s[c * 8 + 2 * e], scale, bf16lo_to_f32(ww[e]));
-                s[c * 8 + 2 * e + 1] = fmaf(s[c * 8 + 2 * e + 1], scale, bf16hi_to_f32(ww[e]));
+                float lo, hi;
+                f2_unpack(f2_fma(f2_pack(s[c * 8 + 2 * e], s[c * 8 + 2 * e + 1]), scale2,
+                                 f2_pack(bf16lo_to_f32(ww[e]), bf16hi_to_f32(ww[e]))), lo, hi);
+                s[c * 8 + 2 * e] = lo;
+                s[c * 8 + 2 * e + 1] = hi;
               }
             }
             // the last step of a query block has now read the whole bias tile: release it, so that the next block's
@@ -321,7 +348,12 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             }
           } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) s[c] *= scale;
+            for (int c = 0; c < 16; ++c) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_pack(s[2 * c], s[2 * c + 1]), scale2), lo, hi);
+              s[2 * c] = lo;
+              s[2 * c + 1] = hi;
+            }
           }
           if (any_dead) {
 #pragma unroll
@@ -333,61 +365,69 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
               }
             }
           }
+          const uint64_t l2e2 = f2_pack(kLog2eF, kLog2eF), nlse2 = f2_pack(neg_lse, neg_lse), ndlt2 = f2_pack(-dlt, -dlt);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 a = *reinterpret_cast<const float4*>(madd + hc * 32 + c * 4);
-            const float p0 = ex2_approx(fmaf(s[c * 4 + 0] + a.x, kLog2eF, neg_lse));
-            const float p1 = ex2_approx(fmaf(s[c * 4 + 1] + a.y, kLog2eF, neg_lse));
-            const float p2 = ex2_approx(fmaf(s[c * 4 + 2] + a.z, kLog2eF, neg_lse));
-            const float p3 = ex2_approx(fmaf(s[c * 4 + 3] + a.w, kLog2eF, neg_lse));
-            const float d0 = p0 * (dp[c * 4 + 0] - dlt), d1 = p1 * (dp[c * 4 + 1] - dlt);
-            const float d2 = p2 * (dp[c * 4 + 2] - dlt), d3 = p3 * (dp[c * 4 + 3] - dlt);
-            acc[hc * 32 + c * 4 + 0] += d0; acc[hc * 32 + c * 4 + 1] += d1;
-            acc[hc * 32 + c * 4 + 2] += d2; acc[hc * 32 + c * 4 + 3] += d3;
+            float x0, x1, x2, x3, d0, d1, d2, d3;
+            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 0], s[c * 4 + 1]), f2_pack(a.x, a.y)), l2e2, nlse2), x0, x1);
+            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 2], s[c * 4 + 3]), f2_pack(a.z, a.w)), l2e2, nlse2), x2, x3);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1), p2 = ex2_approx(x2), p3 = ex2_approx(x3);
+            const uint64_t d01 = f2_mul(f2_pack(p0, p1), f2_add(f2_pack(dp[c * 4 + 0], dp[c * 4 + 1]), ndlt2));
+            const uint64_t d23 = f2_mul(f2_pack(p2, p3), f2_add(f2_pack(dp[c * 4 + 2], dp[c * 4 + 3]), ndlt2));
+            f2_unpack(d01, d0, d1);
+            f2_unpack(d23, d2, d3);
+            float a0, a1, a2, a3;
+            f2_unpack(f2_add(f2_pack(acc[hc * 32 + c * 4 + 0], acc[hc * 32 + c * 4 + 1]), d01), a0, a1);
+            f2_unpack(f2_add(f2_pack(acc[hc * 32 + c * 4 + 2], acc[hc * 32 + c * 4 + 3]), d23), a2, a3);
             pk[hc * 16 + c * 2] = pack_bf16x2(p0, p1); pk[hc * 16 + c * 2 + 1] = pack_bf16x2(p2, p3);
             dk[hc * 16 + c * 2] = pack_bf16x2(d0, d1); dk[hc * 16 + c * 2 + 1] = pack_bf16x2(d2, d3);
+            if (g == gcount - 1) {
+              // last batch row of the query block: the finished dBias sums leave as vector atomics, spread over the
+              // math instead of in one burst
+              if (flush_ok && k0 + half * 64 + hc * 32 + c * 4 < p.sk)
+                red_add_v4(dbias_row + hc * 32 + c * 4, a0, a1, a2, a3);
+            } else {
+              acc[hc * 32 + c * 4 + 0] = a0; acc[hc * 32 + c * 4 + 1] = a1;
+              acc[hc * 32 + c * 4 + 2] = a2; acc[hc * 32 + c * 4 + 3] = a3;
+            }
+          }
+          if (hc == 0 && t > 0) {
+            // the previous step's output GEMMs are complete: its dQ tile can leave TMEM, P/dS can be overwritten
+            CFK_BWD_WAIT(gemm_done, (t - 1) & 1, 803)
+            tc_fence_after();
+            uint32_t r[16];
+            tmem_ld_x16(tmem + lane_addr + kColDq + half * 16, r);
+            tmem_wait_ld();
+            CFK_BWD_WAIT(&dq_free[(t - 1) & 1], (((t - 1) >> 1) & 1) ^ 1, 805)
+            // 128-byte rows, 128-byte swizzle (the reduce's tensor map undoes it): conflict-free 16-byte stores
+            uint8_t* stg = smem + kOffDq + ((t - 1) & 1) * kTileDq;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<float4*>(stg + swz_off(row, half * 4 + c, 128)) =
+                  make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
+                              __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
+          }
+          // this chunk's P and dS into shared memory (64 keys = one 128-byte swizzled row of this thread's half)
+          {
+            uint8_t* p_row = smem + kOffP + half * (kTileBig / 2);
+            uint8_t* ds_row = smem + kOffDs + half * (kTileBig / 2);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t off = swz_off(row, hc * 4 + c, 128);
+              *reinterpret_cast<uint4*>(p_row + off) =
+                  make_uint4(pk[hc * 16 + c * 4], pk[hc * 16 + c * 4 + 1], pk[hc * 16 + c * 4 + 2], pk[hc * 16 + c * 4 + 3]);
+              *reinterpret_cast<uint4*>(ds_row + off) =
+                  make_uint4(dk[hc * 16 + c * 4], dk[hc * 16 + c * 4 + 1], dk[hc * 16 + c * 4 + 2], dk[hc * 16 + c * 4 + 3]);
+            }
           }
         }
-        // the previous step's output GEMMs are complete: its dQ tile can leave TMEM, P/dS can be overwritten
-        if (t > 0) {
-          CFK_BWD_WAIT(gemm_done, (t - 1) & 1, 803)
-          tc_fence_after();
-          uint32_t r[16];
-          tmem_ld_x16(tmem + lane_addr + kColDq + half * 16, r);
-          tmem_wait_ld();
-          // 128-byte rows, 128-byte swizzle (the reduce's tensor map undoes it): conflict-free 16-byte stores
-          uint8_t* stg = smem + kOffDq + ((t - 1) & 1) * kTileDq;
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<float4*>(stg + swz_off(row, half * 4 + c, 128)) =
-                make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
-                            __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
-        }
-        // P and dS rows into shared memory (64 keys = one 128-byte swizzled row of this thread's half)
-        uint8_t* p_row = smem + kOffP + half * (kTileBig / 2);
-        uint8_t* ds_row = smem + kOffDs + half * (kTileBig / 2);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t off = swz_off(row, c, 128);
-          *reinterpret_cast<uint4*>(p_row + off) = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
-          *reinterpret_cast<uint4*>(ds_row + off) = make_uint4(dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
-        }
         fence_proxy_async();
-        if (stid == 0) tma_wait_group_read<0>();  // every earlier dQ reduce has finished reading its staging buffer
-        named_bar_sync(1, kSoftmaxThreads);
-        if (stid == 0 && t > 0 && ok) {
-          const int tp = t - 1, gp = tp % gcount, ip = tp / gcount;
-          tma_reduce_add_4d(&tm_dq, smem + kOffDq + (tp & 1) * kTileDq, 0, ip * kBQ, head, b0 + gp);
-          tma_commit_group();
+        __syncwarp();
+        if (lane == 0) {
+          if (t > 0) mbar_arrive(&dq_staged[(t - 1) & 1]);
+          mbar_arrive(pds_full);
         }
-        if (lane == 0) mbar_arrive(pds_full);
-      }
-      // flush dBias of this query block: the sum over this CTA's batch rows joins the other CTAs' by atomics
-      if (prm.bp.dbias != nullptr && ok && q < p.sq) {
-        float* dst = prm.bp.dbias + (int64_t(head) * p.sq + q) * p.sk + k0 + half * 64;
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          if (k0 + half * 64 + c * 4 < p.sk) red_add_v4(dst + c * 4, acc[c * 4], acc[c * 4 + 1], acc[c * 4 + 2], acc[c * 4 + 3]);
       }
     }
     // ---------------------------------------------------------------- tail: last dQ tile, then dK / dV
@@ -397,6 +437,7 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       uint32_t r[16];
       tmem_ld_x16(tmem + lane_addr + kColDq + half * 16, r);
       tmem_wait_ld();
+      CFK_BWD_WAIT(&dq_free[(nsteps - 1) & 1], (((nsteps - 1) >> 1) & 1) ^ 1, 806)
       uint8_t* stg = smem + kOffDq + ((nsteps - 1) & 1) * kTileDq;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -404,13 +445,8 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             make_float4(__uint_as_float(r[c * 4]) * scale, __uint_as_float(r[c * 4 + 1]) * scale,
                         __uint_as_float(r[c * 4 + 2]) * scale, __uint_as_float(r[c * 4 + 3]) * scale);
       fence_proxy_async();
-      if (stid == 0) tma_wait_group_read<0>();
-      named_bar_sync(1, kSoftmaxThreads);
-      if (stid == 0 && ok) {
-        const int tp = nsteps - 1, gp = tp % gcount, ip = tp / gcount;
-        tma_reduce_add_4d(&tm_dq, smem + kOffDq + (tp & 1) * kTileDq, 0, ip * kBQ, head, b0 + gp);
-        tma_commit_group();
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_staged[(nsteps - 1) & 1]);
       const int key = k0 + row;
       // tcgen05.ld is warp-collective: every lane loads, only the lanes whose key exists store
 #pragma unroll 1
@@ -441,7 +477,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           }
         }
       }
-      if (stid == 0) tma_wait_group<0>();
     }
 #undef CFK_BWD_WAIT
     tc_fence_before();
