@@ -33,7 +33,10 @@ sys.path.insert(0, ROOT)
 
 B, H, S, D = 512, 8, 1024, 32
 METRIC = "biased_attention_fwd_bwd_tflops"
-WORKLOAD = f"msa_row_attention_pair_bias fwd+bwd b={B} h={H} s={S} d={D} layout=seq mask=bernoulli0.95"
+
+
+def workload():
+  return f"msa_row_attention_pair_bias fwd+bwd b={B} h={H} s={S} d={D} layout=seq mask=bernoulli0.95"
 
 
 def flops(b):
@@ -151,7 +154,9 @@ def main():
   ap.add_argument("--warmup", type=int, default=3)
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
   ap.add_argument("--block", type=int, default=1, help="also time one Evoformer block (0 to skip)")
+  ap.add_argument("--batch", type=int, default=B, help="batch rows per GPU (smaller values are for profiler captures only)")
   args = ap.parse_args()
+  globals()["B"] = args.batch
   rank = int(os.environ.get("RANK", "0"))
   world = int(os.environ.get("WORLD_SIZE", "1"))
   local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -163,7 +168,7 @@ def main():
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_sample"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "note": "reference's jnp path needs JAX (absent): CPU port of it, bounded sample"},
+            "config": {"workload": workload(), "note": "reference's jnp path needs JAX (absent): CPU port of it, bounded sample"},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -278,7 +283,7 @@ def main():
         "metric": METRIC, "value": flops(B) * world / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": B * world, "parallelism": f"batch-sharded x{world}, no collective",
+        "config": {"workload": workload(), "global_batch": B * world, "parallelism": f"batch-sharded x{world}, no collective",
                    "l2": "inputs (1.1 GB per rank) exceed the 126 MB L2; no flush between steps",
                    "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
                    "device_status": status,

@@ -1,0 +1,111 @@
+#!/usr/bin/env python
+"""Per-operator timings of the fused Evoformer ops at the pair / MSA sizes of the configs (one JSON line per op).
+
+  python colabfold-kernels_b200/bench_ops.py [--ops all|name,name] [--rows M] [--n N] [--iters K]
+
+HBM-bound ops report GB/s of ALGORITHMIC bytes (every activation read once and written once) and the fraction of
+the measured copy bandwidth; contraction-bound ops report TFLOP/s against the measured dense bf16 peak.  Inputs of
+the default sizes are larger than the 126 MB L2, the host runs ahead of the device (one long sleep kernel first) so
+that the events time kernels only.  `--rows` shrinks the row count for profiler captures.
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+from colabfold_kernels import ops  # noqa: E402
+
+bf = torch.bfloat16
+
+
+def peaks():
+  path = os.path.join(HERE, "..", "MEASURED_PEAKS.json")
+  if os.path.exists(path):
+    d = json.load(open(path))
+    return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+  return 1590.0, 6650.0, "fallback"
+
+
+def timed(fn, iters):
+  for _ in range(3):
+    fn()
+  torch.cuda.synchronize()
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  torch.cuda._sleep(int(4e7))  # lets the host queue every launch before the first one runs
+  e0.record()
+  for _ in range(iters):
+    fn()
+  e1.record()
+  torch.cuda.synchronize()
+  return e0.elapsed_time(e1) / iters
+
+
+def make_cases(m, n, c=128):
+  """name -> (callable, algorithmic bytes, flops).  m rows of c channels; n = residues of the contraction."""
+  dev = "cuda"
+  g = torch.Generator(device=dev).manual_seed(3)
+  rnd = lambda *s: torch.randn(*s, device=dev, generator=g)
+  x = rnd(m, c).to(bf)
+  x_cm = rnd(c, m).to(bf)
+  ones, zeros = torch.ones(c, device=dev), torch.zeros(c, device=dev)
+  w = (rnd(c, c) * c ** -0.5).to(bf)
+  b = torch.zeros(c, device=dev, dtype=bf)
+  wp = (rnd(c, 2 * c) * c ** -0.5).to(bf)
+  bp = torch.zeros(2 * c, device=dev, dtype=bf)
+  w4 = (rnd(4, c, c) * c ** -0.5).to(bf)
+  mask = (torch.rand(m, device=dev, generator=g) < 0.95).to(bf)
+  res = rnd(m, c).to(bf)
+  lw = (rnd(c, 32) * c ** -0.5).to(bf)
+  lb = torch.zeros(32, device=dev, dtype=bf)
+  a = rnd(c, n, n).to(bf)
+  a2 = rnd(c, n, n).to(bf)
+  a8, b8 = a.to(torch.float8_e4m3fn), a2.to(torch.float8_e4m3fn)
+  E = 2  # bytes per bf16
+  return {
+      "layer_norm": (lambda: ops.layer_norm(x, ones, zeros), 2 * m * c * E, 0),
+      "ln_gated_dual_proj": (lambda: ops.ln_gated_dual_proj(x, ones, zeros, wp, bp, wp, bp, mask), m * c * E + 2 * m * c * E + m * E,
+                             2.0 * m * c * 4 * c),
+      "ln_gated_dual_proj_e4m3": (lambda: ops.ln_gated_dual_proj(x, ones, zeros, wp, bp, wp, bp, mask, fp8=True),
+                                  m * c * E + 2 * m * c + m * E, 2.0 * m * c * 4 * c),
+      "gated_dual_proj": (lambda: ops.gated_dual_proj(x, wp, bp, wp, bp, mask), m * c * E + 2 * m * c * E + m * E, 2.0 * m * c * 4 * c),
+      "trimul_epilogue": (lambda: ops.trimul_epilogue(x_cm, x, ones, zeros, w, b, w, b, in_scale=ones, in_offset=zeros, add_input=True),
+                          3 * m * c * E, 4.0 * m * c * c),
+      "ln_projection": (lambda: ops.ln_projection(x, ones, zeros, w4, None), m * c * E + 4 * m * c * E, 2.0 * m * c * 4 * c),
+      "output_projection": (lambda: ops.output_projection(x, w, b, res), 3 * m * c * E, 2.0 * m * c * c),
+      "opm_projection": (lambda: ops.opm_projection(x, ones, zeros, lw, lb, lw, lb, mask), m * c * E + 2 * m * 32 * E + m * E,
+                         2.0 * m * c * 64),
+      "contract_bf16": (lambda: ops.contract(a, a2), 3 * c * n * n * E, 2.0 * c * n ** 3),
+      "contract_e4m3": (lambda: ops.contract(a8, b8), 2 * c * n * n + c * n * n * E, 2.0 * c * n ** 3),
+  }
+
+
+def main():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--ops", default="all")
+  ap.add_argument("--rows", type=int, default=1048576, help="rows M of the [M, 128] activations (1024 x 1024 pair)")
+  ap.add_argument("--n", type=int, default=1024, help="residues of the triangle contraction")
+  ap.add_argument("--iters", type=int, default=20)
+  args = ap.parse_args()
+  if not torch.cuda.is_available():
+    raise SystemExit("bench_ops.py needs a CUDA device: the library has no CPU path")
+  peak_tf, peak_gb, kind = peaks()
+  cases = make_cases(args.rows, args.n)
+  names = list(cases) if args.ops == "all" else args.ops.split(",")
+  for name in names:
+    fn, nbytes, flops = cases[name]
+    ms = timed(fn, args.iters)
+    gbs, tfs = nbytes / ms / 1e6, flops / ms / 1e9
+    tensor_bound = name.startswith("contract")
+    print(json.dumps({
+        "op": name, "rows": args.rows if not tensor_bound else None, "n": args.n if tensor_bound else None, "ms": round(ms, 4),
+        "gb_per_s": round(gbs, 1), "tflop_per_s": round(tfs, 1), "bound": "tensor" if tensor_bound else "hbm",
+        "frac_of_peak": round(tfs / peak_tf if tensor_bound else gbs / peak_gb, 4), "peak_source": kind,
+        "device_status": ops.device_status()}), flush=True)
+
+
+if __name__ == "__main__":
+  main()
