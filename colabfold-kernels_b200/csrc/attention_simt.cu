@@ -136,6 +136,39 @@ __global__ void attn_delta_kernel(const void* out, Strides so, const void* dout,
   if (lane == 0) delta[warp] = s;
 }
 
+// The same for bf16 tensors whose rows are 16-byte aligned and a power-of-two multiple of 8 wide: d/8 threads per row,
+// one 16-byte load of out and of dout each, rows walked in memory order so that a warp reads contiguous bytes.
+__global__ void attn_delta_bf16_vec_kernel(const __nv_bfloat16* __restrict__ out, Strides so,
+                                           const __nv_bfloat16* __restrict__ dout, Strides sdo, float* __restrict__ delta,
+                                           int nb, int h, int sq, int tpr, int heads_inner) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = int64_t(nb) * h * sq * tpr;
+  const int64_t gc = gid < total ? gid : total - 1;  // clamped so that whole warps reach the shuffles
+  const int chunk = int(gc % tpr);
+  const int64_t rowid = gc / tpr;
+  int q, hh, b;
+  if (heads_inner) {  // [b, s, h, d]
+    hh = int(rowid % h);
+    q = int((rowid / h) % sq);
+    b = int(rowid / (int64_t(h) * sq));
+  } else {  // [b, h, s, d]
+    q = int(rowid % sq);
+    hh = int((rowid / sq) % h);
+    b = int(rowid / (int64_t(h) * sq));
+  }
+  const uint4 a = *reinterpret_cast<const uint4*>(out + b * so.b + hh * so.h + int64_t(q) * so.s + chunk * 8);
+  const uint4 g = *reinterpret_cast<const uint4*>(dout + b * sdo.b + hh * sdo.h + int64_t(q) * sdo.s + chunk * 8);
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    s = fmaf(__uint_as_float(aw[e] << 16), __uint_as_float(gw[e] << 16), s);
+    s = fmaf(__uint_as_float(aw[e] & 0xffff0000u), __uint_as_float(gw[e] & 0xffff0000u), s);
+  }
+  for (int off = tpr >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (chunk == 0 && gid < total) delta[(int64_t(b) * h + hh) * sq + q] = s;
+}
+
 // The probability and score gradient of one (query, key) pair, the way the flash backward rebuilds them
 // (tri_flash.py:336-343): masked logits are constants, a fully masked row was the uniform 1/Sk.
 __device__ __forceinline__ void p_and_ds(float dot, float bias, float scale, bool live, bool inb, float lse, float dp,
@@ -300,6 +333,17 @@ int bwd_impl(const AttnBwdProblem& bp, float* delta, cudaStream_t st) {
 void launch_attn_delta_bf16(const AttnBwdProblem& bp, float* delta, cudaStream_t st) {
   const AttnProblem& p = bp.f;
   const int64_t rows = int64_t(p.nb) * p.h * p.sq;
+  const int tpr = p.d / 8;
+  auto vec_ok = [](const void* ptr, const Strides& s) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && s.b % 8 == 0 && s.h % 8 == 0 && s.s % 8 == 0;
+  };
+  if (p.d % 8 == 0 && tpr <= 32 && (tpr & (tpr - 1)) == 0 && vec_ok(p.out, p.so_) && vec_ok(bp.dout, bp.sdo)) {
+    const int64_t threads = rows * tpr;
+    attn_delta_bf16_vec_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(p.out), p.so_, static_cast<const __nv_bfloat16*>(bp.dout), bp.sdo, delta, p.nb, p.h,
+        p.sq, tpr, p.so_.h < p.so_.s);
+    return;
+  }
   attn_delta_kernel<__nv_bfloat16><<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, st>>>(
       p.out, p.so_, bp.dout, bp.sdo, delta, p.nb, p.h, p.sq, p.d);
 }
