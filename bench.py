@@ -279,6 +279,9 @@ def main():
     dominant, dom_ms, dom_flops = ("attention_bwd", bwd, 10.0 * B * H * S * S * D) if bwd >= fwd else \
                                   ("attention_fwd", fwd, 4.0 * B * H * S * S * D)
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    # DRAM bytes of one launch from the ncu captures of the b=96 case (profiles/attention_*_sm100__b96_h8_s1024_d32.md),
+    # scaled by batch: every term but the 16.8 MB bias tile grows with the batch
+    traffic = (868.34e6 if dominant == "attention_bwd" else 226.12e6) * B / 96.0
     line = {
         "metric": METRIC, "value": flops(B) * world / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -295,7 +298,8 @@ def main():
                 "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": achieved / peak_tf, "traffic": None, "peak_source": f"{peak_kind} burst bf16"},
+                     "frac": achieved / peak_tf, "traffic": traffic, "traffic_unit": "bytes per launch (DRAM read + write)",
+                     "peak_source": f"{peak_kind} burst bf16"},
         "clocks": sampler.summary(),
     }
     line["cpu_baseline"] = {k: v for k, v in cpu_arm(3, 1).items() if k != "ms_per_sample"}
