@@ -302,7 +302,8 @@ def main():
                      "peak_source": f"{peak_kind} burst bf16"},
         "clocks": sampler.summary(),
     }
-    line["cpu_baseline"] = {k: v for k, v in cpu_arm(3, 1).items() if k != "ms_per_sample"}
+    if world == 1:  # the CPU arm is reported at N = 1 only
+      line["cpu_baseline"] = {k: v for k, v in cpu_arm(3, 1).items() if k != "ms_per_sample"}
     print(json.dumps(line))
   if world > 1:
     dist.destroy_process_group()
