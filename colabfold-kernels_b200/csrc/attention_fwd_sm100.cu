@@ -230,9 +230,11 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         };
         ok = issue_s();
         if (ok && nsteps > 1) ok = issue_s();
+        // S of step t + 2 goes out as soon as its buffer has been read (early in step t), before this thread blocks on
+        // the P of step t: the group then finds its next scores ready when it finishes a step
         for (int t = 0; t < nsteps && ok; ++t) {
-          ok = issue_pv();
-          if (ok && t + 2 < nsteps) ok = issue_s();
+          if (t + 2 < nsteps) ok = issue_s();
+          if (ok) ok = issue_pv();
         }
       }
       __syncwarp();
