@@ -366,31 +366,36 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             }
           }
           const uint64_t l2e2 = f2_pack(kLog2eF, kLog2eF), nlse2 = f2_pack(neg_lse, neg_lse), ndlt2 = f2_pack(-dlt, -dlt);
+          // Stage by stage over the whole chunk (32 independent elements per stage) instead of element by element:
+          // the exponentials and the arithmetic around them then overlap instead of waiting on one another.
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 8; ++c) {  // exponent arguments, in place of the scores
             const float4 a = *reinterpret_cast<const float4*>(madd + hc * 32 + c * 4);
-            float x0, x1, x2, x3, d0, d1, d2, d3;
-            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 0], s[c * 4 + 1]), f2_pack(a.x, a.y)), l2e2, nlse2), x0, x1);
-            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 2], s[c * 4 + 3]), f2_pack(a.z, a.w)), l2e2, nlse2), x2, x3);
-            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1), p2 = ex2_approx(x2), p3 = ex2_approx(x3);
-            const uint64_t d01 = f2_mul(f2_pack(p0, p1), f2_add(f2_pack(dp[c * 4 + 0], dp[c * 4 + 1]), ndlt2));
-            const uint64_t d23 = f2_mul(f2_pack(p2, p3), f2_add(f2_pack(dp[c * 4 + 2], dp[c * 4 + 3]), ndlt2));
-            f2_unpack(d01, d0, d1);
-            f2_unpack(d23, d2, d3);
-            float a0, a1, a2, a3;
-            f2_unpack(f2_add(f2_pack(acc[hc * 32 + c * 4 + 0], acc[hc * 32 + c * 4 + 1]), d01), a0, a1);
-            f2_unpack(f2_add(f2_pack(acc[hc * 32 + c * 4 + 2], acc[hc * 32 + c * 4 + 3]), d23), a2, a3);
-            pk[hc * 16 + c * 2] = pack_bf16x2(p0, p1); pk[hc * 16 + c * 2 + 1] = pack_bf16x2(p2, p3);
-            dk[hc * 16 + c * 2] = pack_bf16x2(d0, d1); dk[hc * 16 + c * 2 + 1] = pack_bf16x2(d2, d3);
-            if (g == gcount - 1) {
-              // last batch row of the query block: the finished dBias sums leave as vector atomics, spread over the
-              // math instead of in one burst
+            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 0], s[c * 4 + 1]), f2_pack(a.x, a.y)), l2e2, nlse2), s[c * 4 + 0], s[c * 4 + 1]);
+            f2_unpack(f2_fma(f2_add(f2_pack(s[c * 4 + 2], s[c * 4 + 3]), f2_pack(a.z, a.w)), l2e2, nlse2), s[c * 4 + 2], s[c * 4 + 3]);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s[c] = ex2_approx(s[c]);  // p
+#pragma unroll
+          for (int c = 0; c < 16; ++c)  // ds, in place of dp
+            f2_unpack(f2_mul(f2_pack(s[2 * c], s[2 * c + 1]), f2_add(f2_pack(dp[2 * c], dp[2 * c + 1]), ndlt2)), dp[2 * c], dp[2 * c + 1]);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            pk[hc * 16 + c] = pack_bf16x2(s[2 * c], s[2 * c + 1]);
+            dk[hc * 16 + c] = pack_bf16x2(dp[2 * c], dp[2 * c + 1]);
+          }
+          if (g == gcount - 1) {
+            // last batch row of the query block: the finished dBias sums leave as vector atomics during the math
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
               if (flush_ok && k0 + half * 64 + hc * 32 + c * 4 < p.sk)
-                red_add_v4(dbias_row + hc * 32 + c * 4, a0, a1, a2, a3);
-            } else {
-              acc[hc * 32 + c * 4 + 0] = a0; acc[hc * 32 + c * 4 + 1] = a1;
-              acc[hc * 32 + c * 4 + 2] = a2; acc[hc * 32 + c * 4 + 3] = a3;
-            }
+                red_add_v4(dbias_row + hc * 32 + c * 4, acc[hc * 32 + c * 4 + 0] + dp[c * 4 + 0], acc[hc * 32 + c * 4 + 1] + dp[c * 4 + 1],
+                           acc[hc * 32 + c * 4 + 2] + dp[c * 4 + 2], acc[hc * 32 + c * 4 + 3] + dp[c * 4 + 3]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              f2_unpack(f2_add(f2_pack(acc[hc * 32 + 2 * c], acc[hc * 32 + 2 * c + 1]), f2_pack(dp[2 * c], dp[2 * c + 1])),
+                        acc[hc * 32 + 2 * c], acc[hc * 32 + 2 * c + 1]);
           }
           if (hc == 0 && t > 0) {
             // the previous step's output GEMMs are complete: its dQ tile can leave TMEM, P/dS can be overwritten
