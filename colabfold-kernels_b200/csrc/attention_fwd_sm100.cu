@@ -307,28 +307,29 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[grp]);
 
-        // logits t = scale * s + bias (+ mask), row maximum
+        // logits t = scale * s + bias (+ mask), row maximum; packed fp32 pairs: two keys per FMA-pipe instruction
+        const uint64_t scale2 = f2_pack(scale, scale);
         if (prm.has_bias) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const uint4 w = *reinterpret_cast<const uint4*>(bias_tile + (c / 8) * (C::kTileBias / 2) + swz_off(row, c % 8, 128));
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              s[c * 8 + 2 * i] = fmaf(s[c * 8 + 2 * i], scale, bf16lo_to_f32(ww[i]));
-              s[c * 8 + 2 * i + 1] = fmaf(s[c * 8 + 2 * i + 1], scale, bf16hi_to_f32(ww[i]));
-            }
+            for (int i = 0; i < 4; ++i)
+              f2_unpack(f2_fma(f2_pack(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]), scale2,
+                               f2_pack(bf16lo_to_f32(ww[i]), bf16hi_to_f32(ww[i]))), s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < kBK; ++i) s[i] *= scale;
+          for (int i = 0; i < kBK; i += 2) f2_unpack(f2_mul(f2_pack(s[i], s[i + 1]), scale2), s[i], s[i + 1]);
         }
         CFK_SOFTMAX_WAIT(&mask_full[slot], (t / C::kMaskSlots) & 1, 305)
         if (flag_ring[slot] != 0) {
 #pragma unroll
           for (int c = 0; c < kBK / 4; ++c) {
             const float4 a = *reinterpret_cast<const float4*>(mask_ring + slot * 128 + c * 4);
-            s[c * 4 + 0] += a.x; s[c * 4 + 1] += a.y; s[c * 4 + 2] += a.z; s[c * 4 + 3] += a.w;
+            f2_unpack(f2_add(f2_pack(s[c * 4 + 0], s[c * 4 + 1]), f2_pack(a.x, a.y)), s[c * 4 + 0], s[c * 4 + 1]);
+            f2_unpack(f2_add(f2_pack(s[c * 4 + 2], s[c * 4 + 3]), f2_pack(a.z, a.w)), s[c * 4 + 2], s[c * 4 + 3]);
           }
         }
         __syncwarp();
@@ -357,20 +358,29 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           }
         }
         const float neg_m = -m_ref * kLog2eF;
-        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+        // stage by stage over the whole row (128 independent elements per stage), so that the exponentials overlap
         uint32_t pk[kBK / 2];
+        {
+          const uint64_t l2e2 = f2_pack(kLog2eF, kLog2eF), negm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
-        for (int i = 0; i < kBK / 2; i += 2) {
-          const float e0 = ex2_approx(fmaf(s[2 * i], kLog2eF, neg_m));
-          const float e1 = ex2_approx(fmaf(s[2 * i + 1], kLog2eF, neg_m));
-          const float e2 = ex2_approx(fmaf(s[2 * i + 2], kLog2eF, neg_m));
-          const float e3 = ex2_approx(fmaf(s[2 * i + 3], kLog2eF, neg_m));
-          sum0 += e0; sum1 += e1; sum2 += e2; sum3 += e3;
-          pk[i] = pack_bf16x2(e0, e1);
-          pk[i + 1] = pack_bf16x2(e2, e3);
+          for (int i = 0; i < kBK; i += 2) f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), l2e2, negm2), s[i], s[i + 1]);
+#pragma unroll
+          for (int i = 0; i < kBK; ++i) s[i] = ex2_approx(s[i]);
+          uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a, sum_c = sum_a, sum_d = sum_a;
+#pragma unroll
+          for (int i = 0; i < kBK; i += 8) {
+            sum_a = f2_add(sum_a, f2_pack(s[i], s[i + 1]));
+            sum_b = f2_add(sum_b, f2_pack(s[i + 2], s[i + 3]));
+            sum_c = f2_add(sum_c, f2_pack(s[i + 4], s[i + 5]));
+            sum_d = f2_add(sum_d, f2_pack(s[i + 6], s[i + 7]));
+          }
+#pragma unroll
+          for (int i = 0; i < kBK / 2; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
+          float t0, t1;
+          f2_unpack(f2_add(f2_add(sum_a, sum_b), f2_add(sum_c, sum_d)), t0, t1);
+          st_m[g * 128] = m_ref;
+          st_l[g * 128] = l_run * corr + (t0 + t1);
         }
-        st_m[g * 128] = m_ref;
-        st_l[g * 128] = l_run * corr + ((sum0 + sum1) + (sum2 + sum3));
 
         // the previous P V of this buffer must be complete before P is overwritten or O is rescaled
         if (uses > 0) {
