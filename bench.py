@@ -182,6 +182,7 @@ def main():
   torch.cuda.set_device(local_rank)
   dev = torch.device("cuda", local_rank)
   if world > 1:
+    os.environ["NCCL_DEBUG"] = "WARN"  # NCCL's version banner goes to stdout and would sit in front of the JSON line
     dist.init_process_group("nccl", device_id=dev)
   lib = _lib.load()
   bf = torch.bfloat16

@@ -158,7 +158,7 @@ def trimul_epilogue_ln(global_config, dtype):
 
   def fwd(x_cm, x, in_scale, in_offset, ln_scale, ln_offset, wo, bo, wg, bg, keep=None, *, eps=1e-5, add_input=False):
     return ops.trimul_epilogue(x_cm, x, ln_scale, ln_offset, wo, bo, wg, bg, in_scale=in_scale, in_offset=in_offset,
-                               eps=eps, add_input=add_input)
+                               eps=eps, add_input=add_input, keep=keep)
   return grads.differentiable_via(fwd, reference.ref_trimul_epilogue_ln, nondiff=("eps", "add_input"))
 
 
@@ -171,16 +171,19 @@ def ln_projection(global_config, dtype, num_channel, num_output=None):
   from colabfold_kernels import grads, ops, reference
 
   def fwd(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5):
-    return ops.ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps)
+    return ops.ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps, keep=keep)
   return grads.differentiable_via(fwd, reference.ref_ln_projection, nondiff=("eps",))
 
 
 def output_projection(global_config, dtype, num_input, num_output):
-  """-> f(o, w, b, residual=None) or None (fused_ops.py:307-323)."""
+  """-> f(o, w, b, residual=None, keep=None) or None (fused_ops.py:307-323)."""
   if not _half_ok(global_config, dtype) or not _k_ok(num_input) or num_output % 8 != 0:
     return None
   from colabfold_kernels import grads, ops, reference
-  return grads.differentiable_via(ops.output_projection, reference.ref_output_projection)
+
+  def fwd(o, w, b, residual=None, keep=None):
+    return ops.output_projection(o, w, b, residual, keep=keep)
+  return grads.differentiable_via(fwd, reference.ref_output_projection)
 
 
 def opm_projection(global_config, dtype, num_channel, num_outer):

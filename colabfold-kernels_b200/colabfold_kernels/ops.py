@@ -192,8 +192,16 @@ def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, t
   return left, right
 
 
+def _keep(keep):
+  """keep [M] (the rows that matter, transition.py:29-38) -> (contiguous tensor or None, dtype tag)."""
+  if keep is None:
+    return None, 0
+  keep = _c(keep.reshape(-1) if keep.dtype in (torch.float32, torch.bfloat16) else keep.reshape(-1).to(torch.float32))
+  return keep, tag(keep.dtype)
+
+
 def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, in_scale=None, in_offset=None,
-                    eps=1e-5, add_input=False, out=None):
+                    eps=1e-5, add_input=False, out=None, keep=None):
   """(LN(x_cm^T) wo + bo) * sigmoid(g wg + bg) (+ residual | + act); g = act, or LN(act) when in_scale is given."""
   act = _c(act)
   x_cm = _c(x_cm if x_cm.dtype in (torch.bfloat16, torch.float32) else x_cm.to(torch.bfloat16))
@@ -203,37 +211,39 @@ def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=Non
   if out is None:
     out = torch.empty((m, o), dtype=dt, device=act.device)
   res = None if residual is None else _c(residual.to(dt))
+  kp, kt = _keep(keep)
   with torch.cuda.device(act.device):
     _lib.call("cfk_trimul_epilogue", _ptr(x_cm), tag(x_cm.dtype), _ptr(act),
               _ptr(None if in_scale is None else _f32(in_scale)), _ptr(None if in_offset is None else _f32(in_offset)),
               _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(wo.to(dt))), _ptr(_c(bo.to(dt))), _ptr(_c(wg.to(dt))),
-              _ptr(_c(bg.to(dt))), _ptr(res), _ptr(out), m, c, ca, o, float(eps), int(add_input), _stream())
+              _ptr(_c(bg.to(dt))), _ptr(res), _ptr(kp), kt, _ptr(out), m, c, ca, o, float(eps), int(add_input), _stream())
   return out
 
 
-def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f8_scale=1.0):
+def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f8_scale=1.0, keep=None):
   """-> (p [m, g*n] or None, bias [h, m] or None)."""
   x = _c(x)
   dt = x.dtype
   m, a = x.shape
   p_out = b_out = None
+  kp, kt = _keep(keep)
   with torch.cuda.device(x.device):
     if w is not None:
       g, _, n = w.shape
       p_out = torch.empty((m, g * n), dtype=torch.float8_e4m3fn if f8 else dt, device=x.device)
       _lib.call("cfk_ln_projection", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w.to(dt))),
-                _ptr(p_out), m, a, g, n, int(f8), float(f8_scale), float(eps), _stream())
+                _ptr(kp), kt, _ptr(p_out), m, a, g, n, int(f8), float(f8_scale), float(eps), _stream())
     if wb is not None:
       h = wb.shape[1]
       hp = -(-h // 8) * 8
       wbp = torch.nn.functional.pad(wb.to(dt), (0, hp - h)).contiguous()
       b_out = torch.empty((h, m), dtype=dt, device=x.device)
-      _lib.call("cfk_ln_head_bias", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(wbp), _ptr(b_out), m, a,
-                h, hp, float(eps), _stream())
+      _lib.call("cfk_ln_head_bias", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(wbp), _ptr(kp), kt,
+                _ptr(b_out), m, a, h, hp, float(eps), _stream())
   return p_out, b_out
 
 
-def output_projection(o, w, b, residual=None, out=None):
+def output_projection(o, w, b, residual=None, out=None, keep=None):
   o = _c(o)
   dt = o.dtype
   m, k = o.shape
@@ -241,9 +251,10 @@ def output_projection(o, w, b, residual=None, out=None):
   res = None if residual is None else _c(residual.to(dt))
   if out is None:
     out = torch.empty((m, c), dtype=dt, device=o.device)
+  kp, kt = _keep(keep)
   with torch.cuda.device(o.device):
-    _lib.call("cfk_output_projection", _ptr(o), _ptr(_c(w.to(dt))), _ptr(_c(b.to(dt))), _ptr(res), _ptr(out), m, k, c,
-              _stream())
+    _lib.call("cfk_output_projection", _ptr(o), _ptr(_c(w.to(dt))), _ptr(_c(b.to(dt))), _ptr(res), _ptr(kp), kt, _ptr(out),
+              m, k, c, _stream())
   return out
 
 

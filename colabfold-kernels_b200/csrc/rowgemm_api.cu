@@ -100,13 +100,16 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   prm.out[0] = left; prm.out[1] = right;
   prm.ldo = ci; prm.out_dtype = fp8 ? CFK_E4M3 : CFK_BF16; prm.out_scale = 1.f;
   prm.out_channel_major = 1; prm.n_valid = ci;
+  // the mask doubles as the row-block filter: a tile of zeros skips the work, a tile below zero is left unwritten
+  prm.keep = mask; prm.keep_dtype = CFK_BF16;
   return run_chunks(prm, 2 * cpa, wp, wg, 1, p, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void* act, const float* in_scale,
                                    const float* in_offset, const float* ln_scale, const float* ln_offset,
                                    const void* wo, const void* bo, const void* wg, const void* bg, const void* residual,
-                                   void* out, int64_t m, int c, int ca, int o, float eps, int add_input, void* stream) {
+                                   const void* keep, int keep_dtype, void* out, int64_t m, int c, int ca, int o, float eps,
+                                   int add_input, void* stream) {
   if (!x_cm || !act || !ln_scale || !ln_offset || !wo || !bo || !wg || !bg || !out) return CFK_ERR_NULL;
   if (m < 0 || o <= 0 || o % 8 != 0) return CFK_ERR_SHAPE;
   if (!(c == 64 || c == 128) || !k_ok(ca) || (add_input && ca != o)) return CFK_ERR_UNSUPPORTED;
@@ -124,12 +127,14 @@ extern "C" int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void*
   prm.bias[0] = bo; prm.bias[1] = bg; prm.bias_len = o;
   prm.out[0] = out; prm.ldo = o; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f; prm.n_valid = o;
   prm.residual = residual; prm.add_source1 = add_input;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
   // the two weights have different K (c and ca): separate maps inside run_chunks use src[0].k and src[1].k
   return run_chunks(prm, cpa, wo, wg, 1, o, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const float* ln_offset, const void* w, void* p_out,
-                                 int64_t m, int a, int g, int n, int f8, float f8_scale, float eps, void* stream) {
+extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const float* ln_offset, const void* w,
+                                 const void* keep, int keep_dtype, void* p_out, int64_t m, int a, int g, int n, int f8,
+                                 float f8_scale, float eps, void* stream) {
   if (!x || !ln_scale || !ln_offset || !w || !p_out) return CFK_ERR_NULL;
   if (m < 0 || g <= 0 || n <= 0 || n % 8 != 0) return CFK_ERR_SHAPE;
   if (!k_ok(a)) return CFK_ERR_UNSUPPORTED;
@@ -144,11 +149,13 @@ extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const flo
   prm.chunks_per_slot = cps; prm.chunks_per_array = g * cps; prm.bias_slot_stride = 0;
   prm.out[0] = p_out; prm.ldo = int64_t(g) * n; prm.n_valid = g * n;
   prm.out_dtype = f8 ? CFK_E4M3 : CFK_BF16; prm.out_scale = f8 ? f8_scale : 1.f;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
   return run_chunks(prm, g * cps, w, nullptr, g, n, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* ln_offset, const void* wb, void* bias_out,
-                                int64_t m, int a, int h, int h_padded, float eps, void* stream) {
+extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* ln_offset, const void* wb,
+                                const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
+                                float eps, void* stream) {
   if (!x || !ln_scale || !ln_offset || !wb || !bias_out) return CFK_ERR_NULL;
   if (m < 0 || h <= 0 || h > h_padded || h_padded % 8 != 0 || h_padded > 64) return CFK_ERR_SHAPE;
   if (!k_ok(a)) return CFK_ERR_UNSUPPORTED;
@@ -159,11 +166,12 @@ extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const floa
   prm.mode = kModeLinear; prm.dual = 0; prm.n_chunk = 64;
   prm.chunks_per_slot = 1; prm.chunks_per_array = 1;
   prm.out[0] = bias_out; prm.out_channel_major = 1; prm.n_valid = h; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
   return run_chunks(prm, 1, wb, nullptr, 1, h_padded, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, void* out,
-                                     int64_t m, int k, int c, void* stream) {
+extern "C" int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, const void* keep,
+                                     int keep_dtype, void* out, int64_t m, int k, int c, void* stream) {
   if (!o || !w || !b || !out) return CFK_ERR_NULL;
   if (m < 0 || c <= 0 || c % 8 != 0) return CFK_ERR_SHAPE;
   if (!k_ok(k)) return CFK_ERR_UNSUPPORTED;
@@ -178,6 +186,7 @@ extern "C" int cfk_output_projection(const void* o, const void* w, const void* b
   prm.bias[0] = b; prm.bias_len = c;
   prm.out[0] = out; prm.ldo = c; prm.n_valid = c; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
   prm.residual = residual;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
   return run_chunks(prm, cps, w, nullptr, 1, c, static_cast<cudaStream_t>(stream));
 }
 

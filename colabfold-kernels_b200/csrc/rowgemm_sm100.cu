@@ -27,6 +27,7 @@ struct Layout {  // byte offsets inside the (1024-aligned) dynamic shared memory
   int o_bytes;     // bytes per buffer
   int o_arr;       // bytes per output array inside a buffer (two arrays when both accumulators are outputs)
   int no;          // buffers in the ring (1 or 2)
+  int cls;         // int8 [kMaxTilesPerCta] tile classes when rows may be skipped, else -1
   int bars;
   int tmem;
   int total;
@@ -42,6 +43,7 @@ struct KernelArgs {
 };
 
 constexpr int kMaxStages = 4;
+constexpr int kMaxTilesPerCta = 1024;  // with row-block skipping: tile classes of one CTA live in shared memory
 
 __device__ __forceinline__ float act_sigmoid(float x) { return sigmoid_fast(x); }
 
@@ -50,7 +52,8 @@ __device__ __forceinline__ float act_sigmoid(float x) { return sigmoid_fast(x); 
 //   SRC0   source 0 is 0: row-major, 1: channel-major bf16 by TMA, 2: channel-major fp32 by TMA, 3: channel-major by plain loads
 //   OUT    0: row-major through the staging ring, 1: channel-major through the staging ring, 2: straight from registers
 //   E4M3   outputs are e4m3 (else bf16)
-template <int MODE, int DUAL, int SRC0, int OUT, int E4M3>
+//   KEEP   row-block skipping compiled in (a variant without it keeps the epilogue's registers free)
+template <int MODE, int DUAL, int SRC0, int OUT, int E4M3, int KEEP>
 __global__ void __launch_bounds__(kThreadsRg, 1)
 rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ CUtensorMap tw1,
                const __grid_constant__ CUtensorMap tx0, const __grid_constant__ CUtensorMap tx1,
@@ -104,6 +107,34 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  // Row-block skipping: the class of every tile this CTA will visit (1 compute, 0 padding, -1 leave unwritten), worked
+  // out once by all warps so that every role takes the same decision.
+  const int8_t* cls = nullptr;
+  if (KEEP && L.cls >= 0) {
+    int8_t* w = reinterpret_cast<int8_t*>(smem + L.cls);
+    for (int i = warp;; i += kThreadsRg / 32) {
+      const int64_t tile = blockIdx.x + int64_t(i) * gridDim.x;
+      if (tile >= ka.ntiles) break;
+      const int64_t o = tile / ka.tiles_per_outer;
+      const int64_t r0 = (tile % ka.tiles_per_outer) * kRows;
+      float top = -1.f;
+      for (int j = lane; j < kRows; j += 32) {
+        const int64_t r = r0 + j;
+        float v = -1.f;  // rows past the padded extent
+        if (r < p.inner) {
+          const int64_t row = o * p.src[0].stride_outer + r * p.src[0].stride_inner;
+          v = p.keep_dtype == CFK_F32 ? static_cast<const float*>(p.keep)[row]
+                                      : __bfloat162float(static_cast<const __nv_bfloat16*>(p.keep)[row]);
+        } else if (r < p.inner_pad) {
+          v = 0.f;
+        }
+        top = fmaxf(top, v);
+      }
+      for (int off = 16; off > 0; off >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+      if (lane == 0) w[i] = top > 0.f ? 1 : (top == 0.f ? 0 : -1);
+    }
+    cls = w;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -127,10 +158,12 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
             tma_load_3d(smem + L.w[i] + c * L.w_chunk[i] + a * kw * 128, i == 0 ? &tw0 : &tw1, w_full, col + a * 64, 0, slot);
         }
       }
-      uint32_t it = 0;
-      for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x, ++it) {
+      uint32_t it = 0, ti = 0;
+      for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x, ++ti) {
+        if (KEEP && cls != nullptr && cls[ti] != 1) continue;
         const int stage = it % NS;
         if (!mbar_wait_deadline(&a_empty[stage], ((it / NS) & 1) ^ 1)) { report_timeout(p.status, 906); break; }
+        ++it;
         const int o = int(tile / ka.tiles_per_outer);
         const int r0 = int(tile % ka.tiles_per_outer) * kRows;
         uint8_t* base = smem + L.stage0 + stage * L.stage_bytes;
@@ -155,11 +188,13 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
       constexpr uint32_t hi = desc_hi(1024, kSwz128);
       bool ok = mbar_wait_deadline(w_full, 0);
       if (!ok) report_timeout(p.status, 901);
-      uint32_t it = 0, cc = 0;
-      for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x, ++it) {
+      uint32_t it = 0, cc = 0, ti = 0;
+      for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x, ++ti) {
+        if (KEEP && cls != nullptr && cls[ti] != 1) continue;
         const int stage = it % NS;
         ok = mbar_wait_deadline(&a_full[stage], (it / NS) & 1);
         if (!ok) { report_timeout(p.status, 902); break; }
+        ++it;
         for (int c = 0; c < p.chunks && ok; ++c, ++cc) {
           const int buf = cc & 1;
           ok = mbar_wait_deadline(&acc_empty[buf], ((cc >> 1) & 1) ^ 1);
@@ -190,9 +225,10 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     if (lane == 0 && ka.resid_tma != 0) {
       const CUtensorMap* tm = ka.resid_tma == 1 ? &tr : &tx1;
       const int atoms = p.n_chunk / 64;
-      uint32_t cc = 0;
+      uint32_t cc = 0, ti = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x) {
+      for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x, ++ti) {
+        if (KEEP && cls != nullptr && cls[ti] != 1) continue;
         const int o = int(tile / ka.tiles_per_outer);
         const int r0 = int(tile % ka.tiles_per_outer) * kRows;
         for (int c = 0; c < p.chunks; ++c, ++cc) {
@@ -224,13 +260,15 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     const int pt = (warp - 4) * 32 + lane;
     const int trow = pt >> 1, half = pt & 1;
     bool ok = true;
-    uint32_t it = 0;
-    for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x, ++it) {
+    uint32_t it = 0, ti = 0;
+    for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x, ++ti) {
+      if (KEEP && cls != nullptr && cls[ti] != 1) continue;
       const int stage = it % NS;
       if (ok && !mbar_wait_deadline(&raw_full[stage], (it / NS) & 1)) {
         report_timeout(p.status, 904);
         ok = false;
       }
+      ++it;
       const int64_t o = tile / ka.tiles_per_outer;
       const int64_t r = (tile % ka.tiles_per_outer) * kRows + trow;
       const bool valid = r < p.inner;
@@ -398,13 +436,51 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     constexpr bool staged = OUT != 2;
     const bool out_cm = OUT == 1 || (OUT == 2 && p.out_channel_major);
     const bool row_add_direct = !staged && !out_cm && (p.residual != nullptr || p.add_source1);
-    for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x) {
+    uint32_t ti = 0;
+    for (int64_t tile = blockIdx.x; tile < ka.ntiles; tile += gridDim.x, ++ti) {
       const int64_t o = tile / ka.tiles_per_outer;
       const int r0 = int(tile % ka.tiles_per_outer) * kRows;
       const int64_t r = r0 + trow;
       const bool valid = r < p.inner;
       const int64_t src_row = o * p.src[0].stride_outer + r * p.src[0].stride_inner;
       const int64_t out_row = o * p.inner + r;
+      if (KEEP && cls != nullptr && cls[ti] != 1) {
+        // A padding tile gets its result without any of the work, straight from these threads (group g takes the
+        // chunks of its parity): zeros, or the rows that would have been added.  A tile below zero is left alone.
+        if (cls[ti] == 0) {
+          for (int c = grp; c < p.chunks; c += 2) {
+            const int cg = p.chunk0 + c;
+            const int ocol = (cg % p.chunks_per_array) * p.n_chunk;
+            for (int i = 0; i < nouts; ++i) {
+              const int a_idx = two_out ? i : cg / p.chunks_per_array;
+              if (p.out[a_idx] == nullptr) continue;
+              if (out_cm) {
+                if (r >= p.inner_pad) continue;
+                const int64_t plane = p.outer * p.inner_pad;
+                for (int j = 0; j < p.n_chunk && ocol + j < p.n_valid; ++j) {
+                  if (E4M3) static_cast<uint8_t*>(p.out[a_idx])[int64_t(ocol + j) * plane + o * p.inner_pad + r] = 0;
+                  else static_cast<__nv_bfloat16*>(p.out[a_idx])[int64_t(ocol + j) * plane + o * p.inner_pad + r] = __float2bfloat16_rn(0.f);
+                }
+              } else if (valid) {
+                const __nv_bfloat16* add_row =
+                    p.residual != nullptr ? static_cast<const __nv_bfloat16*>(p.residual) + out_row * p.ldo
+                    : p.add_source1 ? static_cast<const __nv_bfloat16*>(p.src[1].x) +
+                                          (o * p.src[1].stride_outer + r * p.src[1].stride_inner) * p.src[1].k
+                                    : nullptr;
+                for (int j = 0; j < p.n_chunk && ocol + j < p.n_valid; j += 8) {
+                  if (E4M3) {
+                    *reinterpret_cast<uint2*>(static_cast<uint8_t*>(p.out[a_idx]) + out_row * p.ldo + ocol + j) = make_uint2(0, 0);
+                  } else {
+                    const uint4 v = add_row != nullptr && i == 0 ? *reinterpret_cast<const uint4*>(add_row + ocol + j) : make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out[a_idx]) + out_row * p.ldo + ocol + j) = v;
+                  }
+                }
+              }
+            }
+          }
+        }
+        continue;
+      }
       float mk = valid ? 1.f : 0.f;
       if (p.rowmask != nullptr && valid) {
         const float m = p.rowmask_dtype == CFK_F32 ? static_cast<const float*>(p.rowmask)[src_row]
@@ -690,8 +766,9 @@ int rowgemm_chunks_that_fit(const RowGemmParams& p) {
   const Plan sp = make_plan(p);
   const int per_chunk = (p.n_chunk / 64) * 128 * (k0 + (p.dual ? k1 : 0));
   // two stages keep loads in flight behind the math
-  int fit = (kSmemBudget - kSmemFixed - 2 * sp.stage_bytes - sp.o_bytes) / per_chunk;
-  if (fit < 1) fit = (kSmemBudget - kSmemFixed - sp.stage_bytes - sp.o_bytes) / per_chunk;
+  const int fixed = kSmemFixed + (p.keep != nullptr ? kMaxTilesPerCta : 0);
+  int fit = (kSmemBudget - fixed - 2 * sp.stage_bytes - sp.o_bytes) / per_chunk;
+  if (fit < 1) fit = (kSmemBudget - fixed - sp.stage_bytes - sp.o_bytes) / per_chunk;
   return fit;
 }
 
@@ -724,7 +801,7 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   ka.out_tma = sp.out_tma;
   ka.resid_tma = sp.resid_tma;
   // shared memory: weights, then as many stages as fit (at least one), a second staging buffer before a third stage
-  const int room = kSmemBudget - kSmemFixed - off;
+  const int room = kSmemBudget - kSmemFixed - off - (p.keep != nullptr ? kMaxTilesPerCta : 0);
   int ns = 0, no = sp.out_tma ? 1 : 0;
   if (room >= 2 * sp.stage_bytes + 2 * sp.o_bytes) {
     no = sp.out_tma ? 2 : 0;
@@ -745,7 +822,13 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   off += no * sp.o_bytes;
   ka.l.bars = off;
   ka.l.tmem = ka.l.bars + 21 * 8;
-  ka.l.total = ka.l.tmem + 16 + 1024;
+  ka.l.cls = -1;
+  int end = ka.l.tmem + 16;
+  if (p.keep != nullptr) {
+    ka.l.cls = end;
+    end += kMaxTilesPerCta;
+  }
+  ka.l.total = end + 1024;
   if (ka.l.total > kSmemBudget) return CFK_ERR_UNSUPPORTED;
 
   // tensor maps of the sources, the outputs and the residual
@@ -801,14 +884,18 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = int(ka.ntiles < sms ? ka.ntiles : sms);
+  if (p.keep != nullptr && (ka.ntiles + grid - 1) / grid > kMaxTilesPerCta) return CFK_ERR_UNSUPPORTED;
   const int src0 = !p.src[0].channel_major ? 0 : sp.direct[0] ? 3 : p.src[0].dtype == CFK_F32 ? 2 : 1;
   const int out = !sp.out_tma ? 2 : p.out_channel_major ? 1 : 0;
   const int e4m3 = p.out_dtype == CFK_E4M3;
   const int key = ((((p.mode * 2) + (p.dual ? 1 : 0)) * 4 + src0) * 3 + out) * 2 + e4m3;
+  const int keep = p.keep != nullptr;
   int rc = CFK_ERR_UNSUPPORTED;
-#define CFK_RG_VARIANT(MODE, DUAL, SRC0, OUT, E4M3)                                                                    \
-  if (key == (((((MODE)*2) + (DUAL)) * 4 + (SRC0)) * 3 + (OUT)) * 2 + (E4M3)) {                                         \
-    auto kern = rowgemm_kernel<MODE, DUAL, SRC0, OUT, E4M3>;                                                           \
+  // KEEP = 1 variants take any call; where a KEEP = 0 twin exists it serves the calls without row-block skipping
+#define CFK_RG_VARIANT(MODE, DUAL, SRC0, OUT, E4M3, KEEP, ALSO_PLAIN)                                                  \
+  if (rc != CFK_OK && key == (((((MODE)*2) + (DUAL)) * 4 + (SRC0)) * 3 + (OUT)) * 2 + (E4M3) &&                         \
+      (keep == (KEEP) || ((KEEP) == 1 && !(ALSO_PLAIN)))) {                                                            \
+    auto kern = rowgemm_kernel<MODE, DUAL, SRC0, OUT, E4M3, KEEP>;                                                     \
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ka.l.total) != cudaSuccess)            \
       return CFK_ERR_LAUNCH;                                                                                           \
     /* the in-kernel register re-split must fit the registers the CTA is launched with, or it would wait forever */  \
@@ -819,26 +906,36 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
     rc = CFK_OK;                                                                                                       \
   }
   // gated dual projection (with or without LayerNorm): row-major or channel-major outputs, bf16 or e4m3
-  CFK_RG_VARIANT(kModeGdp, 1, 0, 0, 0)
-  CFK_RG_VARIANT(kModeGdp, 1, 0, 1, 0)
-  CFK_RG_VARIANT(kModeGdp, 1, 0, 1, 1)
-  CFK_RG_VARIANT(kModeGdp, 1, 0, 2, 0)
-  CFK_RG_VARIANT(kModeGdp, 1, 0, 2, 1)
+  CFK_RG_VARIANT(kModeGdp, 1, 0, 0, 0, 1, 0)
+  CFK_RG_VARIANT(kModeGdp, 1, 0, 1, 0, 1, 0)
+  CFK_RG_VARIANT(kModeGdp, 1, 0, 1, 1, 1, 0)
+  CFK_RG_VARIANT(kModeGdp, 1, 0, 2, 0, 1, 0)
+  CFK_RG_VARIANT(kModeGdp, 1, 0, 2, 1, 1, 0)
   // triangle-multiplication epilogue: channel-major contraction result
-  CFK_RG_VARIANT(kModeEpi, 1, 1, 0, 0)
-  CFK_RG_VARIANT(kModeEpi, 1, 2, 0, 0)
-  CFK_RG_VARIANT(kModeEpi, 1, 3, 0, 0)
-  CFK_RG_VARIANT(kModeEpi, 1, 1, 2, 0)
-  CFK_RG_VARIANT(kModeEpi, 1, 2, 2, 0)
-  CFK_RG_VARIANT(kModeEpi, 1, 3, 2, 0)
+  CFK_RG_VARIANT(kModeEpi, 1, 1, 0, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 1, 0, 0, 1, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 2, 0, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 2, 0, 0, 1, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 3, 0, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 3, 0, 0, 1, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 1, 2, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 1, 2, 0, 1, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 2, 2, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 2, 2, 0, 1, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 3, 2, 0, 0, 1)
+  CFK_RG_VARIANT(kModeEpi, 1, 3, 2, 0, 1, 1)
   // single projections (LayerNorm -> projection, head bias, output projection)
-  CFK_RG_VARIANT(kModeLinear, 0, 0, 0, 0)
-  CFK_RG_VARIANT(kModeLinear, 0, 0, 1, 0)
-  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 0)
-  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 0, 0, 0, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 0, 0, 1, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 1, 0, 0, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 1, 0, 1, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 0, 0, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 0, 1, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 1, 0, 1)
+  CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 1, 1, 1)
   // two projections of one normed tile (outer-product-mean projection)
-  CFK_RG_VARIANT(kModeLinear, 1, 0, 0, 0)
-  CFK_RG_VARIANT(kModeLinear, 1, 0, 2, 0)
+  CFK_RG_VARIANT(kModeLinear, 1, 0, 0, 0, 0, 1)
+  CFK_RG_VARIANT(kModeLinear, 1, 0, 2, 0, 0, 1)
 #undef CFK_RG_VARIANT
   if (rc != CFK_OK) return rc;
   return check_launch();

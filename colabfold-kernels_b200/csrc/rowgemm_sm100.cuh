@@ -50,6 +50,11 @@ struct RowGemmParams {
   int bias_len;                     // entries of each bias vector
   const void* rowmask;              // [rows] in src[0] order (bf16 or fp32 by rowmask_dtype) or nullptr
   int rowmask_dtype;
+  // Row-block skipping (transition.py:29-38 of the reference): keep[rows] in src[0] order, or nullptr.  A 128-row tile
+  // whose largest keep is > 0 is computed as usual; == 0 (padding) it gets zeros - or the residual / raw source-1 rows
+  // where one is added - without any of the work; < 0 it is not written at all.  Rows in [inner, inner_pad) count as 0.
+  const void* keep;
+  int keep_dtype;
   // row-major output: out[i][row * ldo + col0[i] + chunk columns]; chunk c of accumulator i lands in array
   // (c / chunks_per_array), column (c % chunks_per_array) * n_chunk
   void* out[2];

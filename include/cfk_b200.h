@@ -140,6 +140,8 @@ CFK_API int cfk_gated_dual_proj(const void* x, const void* wp, const void* bp, c
  * left, right [p/2, a'].  b > 0: the pair x [a,b,k], mask [a,b] -> [p/2, a, b'] or, with transpose (the pair read
  * transposed, for incoming edges), [p/2, b, a'].  The primed axis is zero-padded to a multiple of `pad`;
  * negative mask values count as zero; fp8 stores saturating unscaled e4m3.  ln_scale, ln_offset fp32 [k].
+ * The mask also filters 128-row tiles: a tile whose mask is all zero gets zeros without its rows being read, a tile
+ * whose mask is below zero everywhere is not written (transition.py:29-38).
  * Replaces ln_gated_dual_proj, tri_mul.py:222-283 (FFI: volta.py:328-334). */
 CFK_API int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, const float* ln_offset, const void* wp,
                                    const void* bp, const void* wg, const void* bg, const void* mask, void* left,
@@ -150,27 +152,34 @@ CFK_API int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, const f
  * x_cm [c,m] channel-major product (x_cm_dtype CFK_BF16 or CFK_F32); act [m,ca] is the gate input: already normed
  * when in_scale == NULL, else the raw module input normed here with in_scale/in_offset; add_input adds act itself
  * (needs ca == o; out may alias act).  residual [m,o] bf16 or NULL.  c is 64 or 128.
+ * keep [m] (keep_dtype CFK_BF16 or CFK_F32) or NULL marks the rows that matter (transition.py:29-38): a 128-row tile
+ * whose largest keep is > 0 is computed in full, one of zeros (padding) gets zeros - or the residual / act rows where
+ * those are added - without the work, one below zero everywhere is not written.  The same holds for every entry
+ * below that takes `keep`.
  * Replaces trimul_epilogue / trimul_epilogue_ln, tri_mul.py:371-438 (FFI: volta.py:345-352). */
 CFK_API int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void* act, const float* in_scale,
                                 const float* in_offset, const float* ln_scale, const float* ln_offset, const void* wo,
-                                const void* bo, const void* wg, const void* bg, const void* residual, void* out,
-                                int64_t m, int c, int ca, int o, float eps, int add_input, void* stream);
+                                const void* bo, const void* wg, const void* bg, const void* residual, const void* keep,
+                                int keep_dtype, void* out, int64_t m, int c, int ca, int o, float eps, int add_input,
+                                void* stream);
 
 /* LayerNorm then the packed attention projection: p[m, g*n + j] = (LN(x) w[g])[m,j]; x [m,a]; w [g,a,n]; no biases.
  * f8 != 0 writes saturating e4m3 of (value * f8_scale) instead of bf16.
  * Replaces ln_projection's slot outputs, packed_attn.py:234-305 (FFI: volta.py:368-383). */
-CFK_API int cfk_ln_projection(const void* x, const float* ln_scale, const float* ln_offset, const void* w, void* p_out,
-                              int64_t m, int a, int g, int n, int f8, float f8_scale, float eps, void* stream);
+CFK_API int cfk_ln_projection(const void* x, const float* ln_scale, const float* ln_offset, const void* w,
+                              const void* keep, int keep_dtype, void* p_out, int64_t m, int a, int g, int n, int f8,
+                              float f8_scale, float eps, void* stream);
 
 /* The per-head bias of the same op, channel-major: bias_out[h, m] = (LN(x) wb)[m, h]; wb [a, h_padded] with
  * h_padded a multiple of 8 (columns past h are ignored).  packed_attn.py:225-229. */
 CFK_API int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* ln_offset, const void* wb,
-                             void* bias_out, int64_t m, int a, int h, int h_padded, float eps, void* stream);
+                             const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
+                             float eps, void* stream);
 
 /* out = o w + b (+ residual); o [m,k]; w [k,c]; b [c]; residual, out [m,c] (out may alias residual).
  * Replaces output_projection, packed_attn.py:352-384 (FFI: volta.py:400-408). */
-CFK_API int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, void* out,
-                                  int64_t m, int k, int c, void* stream);
+CFK_API int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, const void* keep,
+                                  int keep_dtype, void* out, int64_t m, int k, int c, void* stream);
 
 /* left, right = mask[m] * (LN(x) lw + lb), mask[m] * (LN(x) rw + rb); x [m,c]; lw, rw [c,k]; k <= 128.
  * Replaces opm_projection, opm.py:36-59. */
