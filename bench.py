@@ -12,7 +12,7 @@ The JSON line carries:
   value         whole-job TFLOP/s, inputs resident in HBM, CUDA-event timed, max over ranks
   e2e           the same metric through the public selector API with pinned HOST buffers: host->device copies
                 of q, k, v, bias, mask and the cotangent and device->host copies of out, dq, dk, dv, dbias are
-                inside the timed region
+                inside the timed region (the batch streams through in chunks so that copies and kernels overlap)
   roofline      the dominant kernel (the backward) against the measured dense-bf16 peak
   cpu_baseline  the CPU oracle (a port of the reference's fp32 ref_attn and flash backward) timed on this
                 box's host cores on a bounded sample of the same workload
@@ -242,17 +242,49 @@ def main():
   out_host = {n: torch.empty(B, S, H, D, dtype=bf).pin_memory() for n in ("out", "dq", "dk", "dv")}
   out_host["dbias"] = torch.empty(H, S, S, dtype=bf).pin_memory()
 
+  # The step streams the batch through the device in chunks: while chunk c computes, chunk c + 1 is on its way in and the
+  # results of chunk c - 1 are on their way out (three streams, two device slots).  Every chunk is one call of the public
+  # selector callable and one backward through it; dBias accumulates over the chunks in the bias leaf's gradient.
+  n_chunks = 8 if B % 8 == 0 and B >= 64 else 1
+  bc = B // n_chunks
+  s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+  names = ("q", "k", "v", "do", "mask_bias")
+  slots = [{n: torch.empty((bc,) + tuple(host[n].shape[1:]), dtype=bf, device=dev) for n in names} for _ in range(2)]
+  bias_dev = torch.empty(H, S, S, dtype=bf, device=dev)
+  ev_in = [torch.cuda.Event() for _ in range(2)]
+  ev_free = [torch.cuda.Event() for _ in range(2)]
+  for e in ev_free:
+    e.record()
+
   def e2e_step():
-    dq_, dk_, dv_, do_ = (host[n].to(dev, non_blocking=True) for n in ("q", "k", "v", "do"))
-    db_ = host["bias"].to(dev, non_blocking=True)
-    mb_ = host["mask_bias"].to(dev, non_blocking=True)
-    for t in (dq_, dk_, dv_, db_):
-      t.requires_grad_(True)
-    o = kernel(dq_, dk_, dv_, mb_, db_, scale)
-    o.backward(do_)
-    out_host["out"].copy_(o.detach(), non_blocking=True)
-    for n, t in (("dq", dq_), ("dk", dk_), ("dv", dv_), ("dbias", db_)):
-      out_host[n].copy_(t.grad, non_blocking=True)
+    cur = torch.cuda.current_stream()
+    s_in.wait_stream(cur)  # the step before has finished with the bias buffer
+    with torch.cuda.stream(s_in):
+      bias_dev.copy_(host["bias"], non_blocking=True)
+    cur.wait_stream(s_in)
+    bias_leaf = bias_dev.detach().requires_grad_(True)
+    for c in range(n_chunks):
+      sl, rows = c % 2, slice(c * bc, (c + 1) * bc)
+      with torch.cuda.stream(s_in):
+        s_in.wait_event(ev_free[sl])  # the chunk that used this slot has been computed
+        for n in names:
+          slots[sl][n].copy_(host[n][rows], non_blocking=True)
+        ev_in[sl].record(s_in)
+      cur.wait_event(ev_in[sl])
+      qc, kc, vc = (slots[sl][n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+      o = kernel(qc, kc, vc, slots[sl]["mask_bias"], bias_leaf, scale)
+      o.backward(slots[sl]["do"])
+      ev_free[sl].record(cur)
+      s_out.wait_stream(cur)
+      with torch.cuda.stream(s_out):
+        for n, t in (("out", o.detach()), ("dq", qc.grad), ("dk", kc.grad), ("dv", vc.grad)):
+          out_host[n][rows].copy_(t, non_blocking=True)
+          t.record_stream(s_out)
+    s_out.wait_stream(cur)
+    with torch.cuda.stream(s_out):
+      out_host["dbias"].copy_(bias_leaf.grad, non_blocking=True)
+      bias_leaf.grad.record_stream(s_out)
+    cur.wait_stream(s_out)  # the step ends when its last result is in host memory
 
   h2d = sum(host[n].numel() * host[n].element_size() for n in ("q", "k", "v", "do", "bias", "mask_bias"))
   d2h = sum(t.numel() * t.element_size() for t in out_host.values())
@@ -265,6 +297,11 @@ def main():
   t1.record()
   barrier()
   e2e_ms = torch.tensor([t0.elapsed_time(t1) / n_e2e], device=dev)
+  # the streamed step must give what the resident step gives (forward bit for bit; dk through the same kernels)
+  ref_out, ref_lse = ops.attention_fwd(q, k, v, bias, kmask, scale, seq_major=True, want_lse=True)
+  ref_dk = ops.attention_bwd(q, k, v, bias, kmask, ref_out, do, ref_lse, scale, seq_major=True, want_dbias=False)[1]
+  e2e_ok = bool(torch.equal(out_host["out"].to(dev), ref_out)) and bool(torch.equal(out_host["dk"].to(dev), ref_dk))
+  del ref_out, ref_lse, ref_dk
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
   block_ms = evoformer_block_ms(world, rank, dev) if args.block else None
@@ -296,7 +333,8 @@ def main():
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
                        "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms), "chunks": n_chunks,
+                "matches_resident_step": e2e_ok},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf, "traffic": traffic, "traffic_unit": "bytes per launch (DRAM read + write)",
