@@ -81,7 +81,7 @@ class ClockSampler(threading.Thread):
     return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons}
 
 
-def cpu_arm(steps, warmup, sample_b=2):
+def cpu_arm(steps, warmup, sample_b=32):
   """The CPU oracle on a bounded sample (sample_b batch rows of the same heads/seq/head_dim), all host threads."""
   import torch
   import oracle as O
