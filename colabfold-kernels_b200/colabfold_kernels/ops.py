@@ -294,7 +294,13 @@ def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=Non
   rj, e = right.shape[1], right.shape[2]
   a = left.permute(1, 2, 0).reshape(1, ri * c, s).contiguous()       # [(i,c), s]
   b = right.permute(1, 2, 0).reshape(1, rj * e, s).contiguous()      # [(j,e), s]
-  outer = contract(a, b).view(ri, c, rj, e).permute(0, 2, 1, 3).reshape(1, ri * rj, c * e).contiguous()
+  if c == 32 and e == 32 and (s * a.element_size()) % 16 == 0:
+    # the kernel stores the product as [i, j, c, e] itself: no transposed copy of the 2*ri*rj*c*e-byte intermediate
+    outer = torch.empty((1, ri * rj, c * e), dtype=torch.bfloat16, device=left.device)
+    with torch.cuda.device(left.device):
+      _lib.call("cfk_opm_outer_product", _ptr(a), _ptr(b), _ptr(outer), ri, rj, s, tag(a.dtype), _stream())
+  else:
+    outer = contract(a, b).view(ri, c, rj, e).permute(0, 2, 1, 3).reshape(1, ri * rj, c * e).contiguous()
   wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
   x = contract(outer, wt).view(ri, rj, w.shape[1])
   norm = mask_left.float().t() @ mask_right.float()

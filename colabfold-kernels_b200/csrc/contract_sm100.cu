@@ -33,6 +33,7 @@ struct ContractParams {
   int is_f8;
   float alpha;
   int* status;
+  int opm;              // 1: rows are (i, 32 channels), columns (j, 32 channels); the product is stored as [i, j, 32, 32]
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -159,14 +160,24 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]) * prm.alpha, __uint_as_float(r[q * 8 + 5]) * prm.alpha);
             w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]) * prm.alpha, __uint_as_float(r[q * 8 + 7]) * prm.alpha);
             const int chunk = cc * 4 + q;  // 16-byte chunk inside the 256-byte half row
-            *reinterpret_cast<uint4*>(stage + (chunk / 8) * (kTM * 128) + swz_off(row, chunk % 8, 128)) = w;
+            if (prm.opm)  // four [128 rows x 32 columns] sub-tiles, one per residue j: 64-byte swizzled rows
+              *reinterpret_cast<uint4*>(stage + (chunk / 4) * (kTM * 64) + swz_off(row, chunk % 4, 64)) = w;
+            else
+              *reinterpret_cast<uint4*>(stage + (chunk / 8) * (kTM * 128) + swz_off(row, chunk % 8, 128)) = w;
           }
         }
         fence_proxy_async();
         named_bar_sync(1, 128);
         if (issuer && ok) {
-          tma_store_3d(&tm_o, stage, j0 + half * 128, i0, c);
-          tma_store_3d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0, c);
+          if (prm.opm) {
+            // 4-D map (e, c, j, i) in memory order: a sub-tile is the 32 x 32 blocks of one j for the tile's four i
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub)
+              tma_store_4d(&tm_o, stage + sub * (kTM * 64), 0, 0, (j0 + half * 128) / 32 + sub, i0 / 32);
+          } else {
+            tma_store_3d(&tm_o, stage, j0 + half * 128, i0, c);
+            tma_store_3d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0, c);
+          }
           tma_commit_group();
         }
       }
@@ -189,8 +200,10 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 
 using namespace cfk;
 
-extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
-                            void* stream) {
+namespace {
+// opm_ri > 0: a is [(opm_ri x 32), k], b [(opm_rj x 32), k] and the product is stored as out[opm_ri, opm_rj, 32, 32]
+int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha, int opm_ri,
+                  int opm_rj, void* stream) {
   if (a == nullptr || b == nullptr || out == nullptr) return CFK_ERR_NULL;
   if (c <= 0 || i <= 0 || j <= 0 || k <= 0) return CFK_ERR_SHAPE;
   if (dtype != CFK_BF16 && dtype != CFK_E4M3) return CFK_ERR_DTYPE;
@@ -213,14 +226,22 @@ extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int 
     int rc = make_tensor_map(&tb, b, dtype, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  {
+  if (opm_ri > 0) {
+    // out [ri, rj, 32, 32] in memory order (e, c, j, i): a store box of 32 e x 32 c x 1 j x 4 i is one [128 rows][32
+    // columns] sub-tile of the staging buffer
+    uint64_t dims[4] = {32, 32, uint64_t(opm_rj), uint64_t(opm_ri)};
+    uint64_t str[3] = {32 * 2, 32 * 32 * 2, uint64_t(opm_rj) * 32 * 32 * 2};
+    uint32_t box[4] = {32, 32, 1, 4};
+    int rc = make_tensor_map(&to, out, CFK_BF16, 4, dims, str, box, 64);
+    if (rc != CFK_OK) return rc;
+  } else {
     uint64_t dims[3] = {uint64_t(j), uint64_t(i), uint64_t(c)};
     uint64_t str[2] = {uint64_t(j) * 2, uint64_t(i) * j * 2};
     uint32_t box[3] = {64, kTM, 1};
     int rc = make_tensor_map(&to, out, CFK_BF16, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word()};
+  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   static bool attr_set = false;
   if (!attr_set) {
@@ -235,4 +256,15 @@ extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int 
   const int grid = int(ntiles < sms ? ntiles : sms);
   contract_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(ta, tb, to, prm);
   return check_launch();
+}
+}  // namespace
+
+extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
+                            void* stream) {
+  return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, stream);
+}
+
+extern "C" int cfk_opm_outer_product(const void* a, const void* b, void* out, int ri, int rj, int s, int dtype, void* stream) {
+  if (ri <= 0 || rj <= 0 || s <= 0) return CFK_ERR_SHAPE;
+  return contract_impl(a, b, out, 1, ri * 32, rj * 32, s, dtype, 1.0f, ri, rj, stream);
 }

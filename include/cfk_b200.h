@@ -125,6 +125,13 @@ CFK_API int cfk_trim_limits(const uint8_t* kmask, int32_t* limits, int batch, in
 CFK_API int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
                          void* stream);
 
+/* The outer product of the outer-product-mean over the MSA depth, for 32-channel projections:
+ * out[i, j, c, e] = sum_s a[i*32 + c, s] * b[j*32 + e, s]; a [ri*32, s], b [rj*32, s] in `dtype` (CFK_BF16 or CFK_E4M3),
+ * out [ri, rj, 32, 32] bf16 - the layout the output linear of the module contracts over (c, e) without a transposed
+ * copy.  s * itemsize must be a multiple of 16.  The reference has the shallow forms only (opm_outer, opm.py:122-168:
+ * the same sum for 16 MSA rows); the deep form is left to XLA inside ColabFold. */
+CFK_API int cfk_opm_outer_product(const void* a, const void* b, void* out, int ri, int rj, int s, int dtype, void* stream);
+
 /* ---- Projection family (bf16; K, the contracted width, must be 64, 128 or 256; unsupported widths return
  * CFK_ERR_UNSUPPORTED and the caller runs its own path, as the reference's selectors return None) -----------
  *

@@ -53,3 +53,23 @@ def test_triangle_einsum_orders():
   out = ops.contract(r.permute(2, 1, 0).contiguous().cuda(), l.permute(2, 1, 0).contiguous().cuda())
   ref = torch.einsum("kjc,kic->cij", l.float(), r.float())
   assert O.rel_err(out.cpu().float(), ref) <= 8e-3
+
+
+@pytest.mark.parametrize("s,r", [(24, 10), (64, 36), (16, 130)])
+def test_outer_product_mean_matches_oracle(s, r):
+  """Deep-MSA outer product mean through the [i, j, c, e] store of the contraction kernel (row counts that are not
+  multiples of the 4 x 8 residues a tile holds exercise the clipping of the 4-D store)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(s + r)
+  mk = lambda *sh, sc=.5: torch.from_numpy((rng.standard_normal(sh) * sc).astype(np.float32)).to(torch.bfloat16)
+  mask = torch.from_numpy((rng.random((s, r)) > .1).astype(np.float32))
+  left, right = mk(s, r, 32) * mask[..., None].to(torch.bfloat16), mk(s, r, 32) * mask[..., None].to(torch.bfloat16)
+  w, bias, res = mk(32 * 32, 128, sc=1 / 32), mk(128, sc=.1), mk(r, r, 128)
+  ref = O.ref_opm_deep(left, right, mask, w, bias, res)
+  got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda())
+  assert ops.device_status() == 0
+  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
+  # row-sharded use: a slice of the left rows against all of the right
+  part = ops.outer_product_mean(left[:, 2:7].cuda(), right.cuda(), mask[:, 2:7].cuda(), mask.cuda(), w.cuda(), bias.cuda(),
+                                residual=res[2:7].cuda())
+  assert torch.equal(part, got[2:7])
