@@ -38,6 +38,7 @@ struct KernelArgs {
   Layout l;
   int64_t ntiles, tiles_per_outer;
   int direct[2];  // channel-major source i is gathered with plain loads instead of TMA
+  int stream_w;   // weights do not stay resident: chunk cc uses slot cc % 2 of a two-chunk ring, refilled from L2
   int out_tma;    // outputs leave through the staging ring and TMA stores (else straight from registers)
   int resid_tma;  // 0: none (or plain loads); 1: residual chunk by TMA (map tr); 2: raw rows of source 1 by TMA (map tx1)
 };
@@ -78,6 +79,8 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
   uint64_t* acc_empty = acc_full + 2;            // [2]
   uint64_t* o_full = acc_empty + 2;              // [2] residual chunk landed in the staging buffer
   uint64_t* o_empty = o_full + 2;                // [2] the TMA store out of the buffer has read it
+  uint64_t* ws_full = o_empty + 2;               // [2] streamed weights: chunk landed in ring slot
+  uint64_t* ws_empty = ws_full + 2;              // [2] ... and the MMAs reading it have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsrc = p.src[1].x != nullptr ? 2 : 1;
@@ -96,6 +99,8 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
       mbar_init(&acc_empty[i], 8);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 1);
+      mbar_init(&ws_full[i], 1);
+      mbar_init(&ws_empty[i], 1);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tw0);
@@ -147,8 +152,8 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
       const int atoms = p.n_chunk / 64;
       uint32_t bytes = 0;
       for (int i = 0; i < nacc; ++i) bytes += uint32_t(p.chunks) * L.w_chunk[i];
-      mbar_arrive_expect_tx(w_full, bytes);
-      for (int i = 0; i < nacc; ++i) {
+      if (!ka.stream_w) mbar_arrive_expect_tx(w_full, bytes);
+      for (int i = 0; i < nacc && !ka.stream_w; ++i) {
         const int kw = p.src[(i == 1 && nsrc == 2) ? 1 : 0].k;
         for (int c = 0; c < p.chunks; ++c) {
           const int cg = p.chunk0 + c;
@@ -186,7 +191,7 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     if (lane == 0) {
       const uint32_t idesc = make_idesc(kRows, uint32_t(p.n_chunk), 1, 1, 0, 1);
       constexpr uint32_t hi = desc_hi(1024, kSwz128);
-      bool ok = mbar_wait_deadline(w_full, 0);
+      bool ok = ka.stream_w ? true : mbar_wait_deadline(w_full, 0);
       if (!ok) report_timeout(p.status, 901);
       uint32_t it = 0, cc = 0, ti = 0;
       for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x, ++ti) {
@@ -199,12 +204,17 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
           const int buf = cc & 1;
           ok = mbar_wait_deadline(&acc_empty[buf], ((cc >> 1) & 1) ^ 1);
           if (!ok) { report_timeout(p.status, 903); break; }
+          const int wslot = ka.stream_w ? int(cc & 1) : c;  // streamed: ring slot of this chunk
+          if (ka.stream_w) {
+            ok = mbar_wait_deadline(&ws_full[wslot], (cc >> 1) & 1);
+            if (!ok) { report_timeout(p.status, 909); break; }
+          }
           tc_fence_after();
           for (int i = 0; i < nacc; ++i) {
             const int s = (i == 1 && nsrc == 2) ? 1 : 0;
             const int kw = p.src[s].k;
             const uint32_t a_lo = desc_lo(smem_u32(smem + L.stage0 + stage * L.stage_bytes + L.a[s]), 16);
-            const uint32_t w_lo = desc_lo(smem_u32(smem + L.w[i] + c * L.w_chunk[i]), uint32_t(kw) * 128);
+            const uint32_t w_lo = desc_lo(smem_u32(smem + L.w[i] + wslot * L.w_chunk[i]), uint32_t(kw) * 128);
             const uint32_t d = tmem + buf * 256 + i * 128;
             // one 64-column atom of A per outer iteration, four K = 16 steps inside it
             uint32_t al = a_lo, wl = w_lo;
@@ -214,9 +224,37 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
               for (int q = 0; q < 4; ++q) mma_f16_ss2(d, al + q * 2, hi, wl + q * 128, hi, idesc, (at | q) != 0);
             }
           }
+          if (ka.stream_w) mma_commit(&ws_empty[wslot]);
           mma_commit(&acc_full[buf]);
         }
         if (ok) mma_commit(&a_empty[stage]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ------------------------------------------------------------------ weight streamer: chunk -> two-slot ring (from L2)
+    if (lane == 0 && ka.stream_w) {
+      const int atoms = p.n_chunk / 64;
+      uint32_t cc = 0, ti = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < ka.ntiles && ok; tile += gridDim.x, ++ti) {
+        if (KEEP && cls != nullptr && cls[ti] != 1) continue;
+        for (int c = 0; c < p.chunks; ++c, ++cc) {
+          const int wslot = cc & 1;
+          if (!mbar_wait_deadline(&ws_empty[wslot], ((cc >> 1) & 1) ^ 1)) { report_timeout(p.status, 910); ok = false; break; }
+          uint32_t bytes = 0;
+          for (int i = 0; i < nacc; ++i) bytes += L.w_chunk[i];
+          mbar_arrive_expect_tx(&ws_full[wslot], bytes);
+          const int cg = p.chunk0 + c;
+          const int slot = cg / p.chunks_per_slot;
+          const int col = (cg % p.chunks_per_slot) * p.n_chunk;
+          for (int i = 0; i < nacc; ++i) {
+            const int kw = p.src[(i == 1 && nsrc == 2) ? 1 : 0].k;
+            for (int a = 0; a < atoms; ++a)
+              tma_load_3d(smem + L.w[i] + wslot * L.w_chunk[i] + a * kw * 128, i == 0 ? &tw0 : &tw1, &ws_full[wslot], col + a * 64, 0,
+                          slot);
+          }
+        }
       }
     }
     __syncwarp();
@@ -756,7 +794,7 @@ Plan make_plan(const RowGemmParams& p) {
 }
 
 constexpr int kSmemBudget = 232448;
-constexpr int kSmemFixed = 1024 /*alignment slack*/ + 21 * 8 + 32;
+constexpr int kSmemFixed = 1024 /*alignment slack*/ + 25 * 8 + 32;
 
 }  // namespace
 
@@ -770,6 +808,15 @@ int rowgemm_chunks_that_fit(const RowGemmParams& p) {
   int fit = (kSmemBudget - fixed - 2 * sp.stage_bytes - sp.o_bytes) / per_chunk;
   if (fit < 1) fit = (kSmemBudget - fixed - sp.stage_bytes - sp.o_bytes) / per_chunk;
   return fit;
+}
+
+bool rowgemm_stream_fits(const RowGemmParams& p) {
+  const int nsrc = p.src[1].x != nullptr ? 2 : 1;
+  const int k0 = p.src[0].k, k1 = nsrc == 2 ? p.src[1].k : k0;
+  const Plan sp = make_plan(p);
+  const int per_chunk = (p.n_chunk / 64) * 128 * (k0 + (p.dual ? k1 : 0));
+  const int fixed = kSmemFixed + (p.keep != nullptr ? kMaxTilesPerCta : 0);
+  return kSmemBudget - fixed - 2 * per_chunk - sp.stage_bytes - sp.o_bytes >= 0;
 }
 
 int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st) {
@@ -786,11 +833,12 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   for (int i = 0; i < nacc; ++i)
     if (p.bias[i] != nullptr && !ptr_aligned16(p.bias[i])) return CFK_ERR_ALIGN;
   int off = 0;
+  ka.stream_w = prm.stream_weights;
   for (int i = 0; i < 2; ++i) {
     const int kw = p.src[(i == 1 && nsrc == 2) ? 1 : 0].k;
     ka.l.w[i] = off;
     ka.l.w_chunk[i] = (p.n_chunk / 64) * kw * 128;
-    if (i < nacc) off += p.chunks * ka.l.w_chunk[i];
+    if (i < nacc) off += (ka.stream_w ? 2 : p.chunks) * ka.l.w_chunk[i];
   }
   const Plan sp = make_plan(p);
   for (int i = 0; i < 2; ++i) {
@@ -821,7 +869,7 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   ka.l.no = no > 0 ? no : 1;
   off += no * sp.o_bytes;
   ka.l.bars = off;
-  ka.l.tmem = ka.l.bars + 21 * 8;
+  ka.l.tmem = ka.l.bars + 25 * 8;
   ka.l.cls = -1;
   int end = ka.l.tmem + 16;
   if (p.keep != nullptr) {

@@ -44,6 +44,7 @@ struct RowGemmParams {
   int n_chunk;                      // columns per accumulator and chunk: 16..128, multiple of 16
   int chunks;                       // chunks handled per tile (weights of all of them stay resident)
   int chunk0;                       // global index of this launch's first chunk (launches may split the chunk list)
+  int stream_weights;               // 1: all chunks in one launch, their weights streamed through a two-chunk ring
   int chunks_per_slot;              // global chunk c -> weight slot c / chunks_per_slot, column (c % chunks_per_slot) * n_chunk
   int bias_slot_stride;             // bias index = slot * bias_slot_stride + column
   const void* bias[2];              // bf16 [N] per accumulator or nullptr (indexed by absolute output column)
@@ -69,7 +70,8 @@ struct RowGemmParams {
   int* status;
 };
 
-int rowgemm_chunks_that_fit(const RowGemmParams& prm);  // chunks whose weights fit beside two pipeline stages
+int rowgemm_chunks_that_fit(const RowGemmParams& prm);
+bool rowgemm_stream_fits(const RowGemmParams& prm);    // room for a two-chunk weight ring, one stage and the staging buffer  // chunks whose weights fit beside two pipeline stages
 int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st);
 int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
 
