@@ -319,7 +319,7 @@ def main():
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
     # DRAM bytes of one launch from the ncu captures of the b=96 case (profiles/attention_*_sm100__b96_h8_s1024_d32.md),
     # scaled by batch: every term but the 16.8 MB bias tile grows with the batch
-    traffic = (868.34e6 if dominant == "attention_bwd" else 226.12e6) * B / 96.0
+    traffic = (862.02e6 if dominant == "attention_bwd" else 235.96e6) * B / 96.0
     line = {
         "metric": METRIC, "value": flops(B) * world / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
