@@ -195,13 +195,27 @@ def opm_projection(global_config, dtype, num_channel, num_outer):
 
 
 def opm_update(global_config, dtype, num_inner, num_output):
-  """The shallow-MSA pair update (fused_ops.py:326-342) has no kernel in this build: the caller runs its own path."""
-  return None
+  """-> f(lhs, t, bias, norm, residual=None, *, eps) or None: the shallow outer product mean's whole pair update
+  (fused_ops.py:326-342): one tensor-core GEMM and the normalising tail.  Widths as the reference's `supported`
+  (opm.py:88-90): K a multiple of 32, F a power of two from 16 to 128."""
+  if not _half_ok(global_config, dtype):
+    return None
+  if num_inner % 32 != 0 or num_output & (num_output - 1) or not 16 <= num_output <= 128:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.opm_update, reference.ref_opm_update, nondiff=("eps",))
 
 
 def opm_outer(global_config, dtype, rows, num_inner, d, num_output):
-  """The 16-row outer product (fused_ops.py:345-361) has no kernel in this build: the caller runs its own path."""
-  return None
+  """-> f(left, right, w) or None: the outer product mean in AF2's own order on 16 rows (fused_ops.py:345-361): the rows'
+  outer product (stored by the contraction kernel in the layout the output weights read), then w.  Shapes as the
+  reference's `outer_supported` (opm.py:142-144)."""
+  if not _half_ok(global_config, dtype):
+    return None
+  if rows != 16 or num_inner % 16 != 0 or d % 4 != 0 or num_output & (num_output - 1) or not 16 <= num_output <= 128:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.opm_outer, reference.ref_opm_outer)
 
 
 def transition(global_config, dtype, num_channel, num_intermediate):

@@ -286,10 +286,8 @@ def opm_finish(x, bias, norm, residual=None, eps=1e-3, out=None):
   return out
 
 
-def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
-  """Deep-MSA outer product mean from the masked projections left [s, ri, c], right [s, rj, c]: two tensor-core GEMMs
-  (the outer product over the MSA depth, rounded to bf16 as the reference's opm_outer does, opm.py:124-134; then the
-  output weights w [c*c, f]) and the normalising tail -> [ri, rj, f].  ri < rj when the pair is row-sharded."""
+def _outer_product(left, right):
+  """sum_s left[s,i,c] right[s,j,e] -> [i*j, c*e] bf16, rounded as the reference's opm_outer writes it (opm.py:124-134)."""
   s, ri, c = left.shape
   rj, e = right.shape[1], right.shape[2]
   a = left.permute(1, 2, 0).reshape(1, ri * c, s).contiguous()       # [(i,c), s]
@@ -299,8 +297,38 @@ def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=Non
     outer = torch.empty((1, ri * rj, c * e), dtype=torch.bfloat16, device=left.device)
     with torch.cuda.device(left.device):
       _lib.call("cfk_opm_outer_product", _ptr(a), _ptr(b), _ptr(outer), ri, rj, s, tag(a.dtype), _stream())
-  else:
-    outer = contract(a, b).view(ri, c, rj, e).permute(0, 2, 1, 3).reshape(1, ri * rj, c * e).contiguous()
+    return outer
+  return contract(a, b).view(ri, c, rj, e).permute(0, 2, 1, 3).reshape(1, ri * rj, c * e).contiguous()
+
+
+def opm_outer(left, right, w):
+  """The outer product mean in AF2's own order (opm.py:147-168): left [rows, B, C], right [rows, D, E], w [C*E, F] ->
+  [B, D, F] in left's dtype; the rows' outer product rounded to left's dtype, then w over (c, e)."""
+  _, bdim, c = left.shape
+  ddim, e = right.shape[1], right.shape[2]
+  outer = _outer_product(left, right)
+  wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
+  return contract(outer, wt).view(bdim, ddim, w.shape[1])
+
+
+def opm_update(lhs, t, bias, norm, residual=None, eps=1e-3):
+  """The shallow outer product mean's pair update (opm.py:93-119): lhs [B, K], t [K, D, F], bias [F], norm [B, D],
+  residual [B, D, F] -> (lhs . t + bias) / (eps + norm) (+ residual), [B, D, F]."""
+  bdim, k = lhs.shape
+  ddim, f = t.shape[1], t.shape[2]
+  dt = lhs.dtype
+  tt = t.to(dt).reshape(k, ddim * f).t().contiguous().view(1, ddim * f, k)
+  x = contract(_c(lhs).view(1, bdim, k), tt).view(bdim, ddim, f)
+  return opm_finish(x, bias, norm, None if residual is None else residual.to(dt), eps)
+
+
+def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+  """Deep-MSA outer product mean from the masked projections left [s, ri, c], right [s, rj, c]: two tensor-core GEMMs
+  (the outer product over the MSA depth, rounded to bf16 as the reference's opm_outer does, opm.py:124-134; then the
+  output weights w [c*c, f]) and the normalising tail -> [ri, rj, f].  ri < rj when the pair is row-sharded."""
+  ri, c = left.shape[1], left.shape[2]
+  rj, e = right.shape[1], right.shape[2]
+  outer = _outer_product(left, right)
   wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
   x = contract(outer, wt).view(ri, rj, w.shape[1])
   norm = mask_left.float().t() @ mask_right.float()

@@ -87,6 +87,20 @@ def ref_opm_projection(x, ln_scale, ln_offset, lw, lb, rw, rb, mask, *, eps=1e-5
   return mv * (y @ _f(lw) + _f(lb)), mv * (y @ _f(rw) + _f(rb))
 
 
+def ref_opm_update(lhs, t, bias, norm, residual=None, *, eps=1e-3):
+  """opm.py:116-119."""
+  out = torch.einsum("bk,kdf->bdf", _f(lhs), _f(t)) + _f(bias)
+  out = out / (eps + _f(norm))[..., None]
+  return out if residual is None else out + _f(residual)
+
+
+def ref_opm_outer(left, right, w):
+  """opm.py:165-168."""
+  act = torch.einsum("abc,ade->bced", _f(left), _f(right))
+  act = act.reshape(act.shape[0], -1, act.shape[-1])
+  return torch.einsum("bkd,kf->bdf", act, _f(w))
+
+
 def ref_transition(x, ln_scale, ln_offset, w1, b1, w2, b2, keep=None, *, eps=1e-5, add_input=False):
   """transition.py:141-146."""
   xf = _f(x)

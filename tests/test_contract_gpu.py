@@ -73,3 +73,33 @@ def test_outer_product_mean_matches_oracle(s, r):
   part = ops.outer_product_mean(left[:, 2:7].cuda(), right.cuda(), mask[:, 2:7].cuda(), mask.cuda(), w.cuda(), bias.cuda(),
                                 residual=res[2:7].cuda())
   assert torch.equal(part, got[2:7])
+
+
+def test_shallow_opm_forms_match_the_reference_fixtures(golden):
+  """opm_outer and opm_update through the selectors against the reference's own ref_* outputs (tests/golden)."""
+  from colabfold_kernels import dispatch, fused_ops, ops
+  cfg = dispatch()
+  bf16 = lambda a: torch.from_numpy(np.asarray(a, dtype=np.float32)).to(torch.bfloat16).cuda()
+  g = golden("opm_outer")
+  rows, b, c = g["left"].shape
+  d, e = g["right"].shape[1:]
+  f = g["w"].shape[1]
+  sel = fused_ops.opm_outer(cfg, torch.bfloat16, rows, c, d, f)
+  assert callable(sel)
+  got = sel(bf16(g["left"]), bf16(g["right"]), bf16(g["w"]))
+  ref = O.ref_opm_outer(bf16(g["left"]).cpu(), bf16(g["right"]).cpu(), bf16(g["w"]).cpu())
+  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
+  assert O.rel_err(got.cpu().float(), torch.from_numpy(np.asarray(g["out"], dtype=np.float32))) <= 5e-2
+  g = golden("opm_update")
+  k = g["lhs"].shape[1]
+  f = g["t"].shape[2]
+  sel = fused_ops.opm_update(cfg, torch.bfloat16, k, f)
+  assert callable(sel)
+  got = sel(bf16(g["lhs"]), bf16(g["t"]), bf16(g["bias"]), torch.from_numpy(np.asarray(g["norm"], dtype=np.float32)).cuda(),
+            bf16(g["residual"]))
+  ref = O.ref_opm_update(bf16(g["lhs"]).cpu(), bf16(g["t"]).cpu(), bf16(g["bias"]).cpu(),
+                         torch.from_numpy(np.asarray(g["norm"], dtype=np.float32)), bf16(g["residual"]).cpu())
+  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
+  assert fused_ops.opm_outer(cfg, torch.bfloat16, 12, c, d, f) is None       # not 16 rows: the caller's own path
+  assert fused_ops.opm_update(cfg, torch.bfloat16, 40, 128) is None           # K not a multiple of 32
+  assert ops.device_status() == 0
