@@ -109,9 +109,10 @@ def cpu_arm(steps, warmup, sample_b=32):
                     f"median of {len(times)}", "ms_per_sample": sec * 1e3}
 
 
-def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024):
+def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False):
   """Second metric: one Evoformer block (inference wiring of the fused ops) at N_seq=512, N_res=1024, device-timed,
-  max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed)."""
+  max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed).  fp8_trimul: the
+  reference's opt-in e4m3 triangle contraction (half the bytes of the operand the ranks exchange)."""
   import torch
   import torch.distributed as dist
   from colabfold_kernels import evoformer
@@ -124,12 +125,12 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024):
   params = evoformer.init_params(device=dev)
   K = evoformer.cuda_kernels()
   if world > 1:
-    blk = evoformer.ShardedBlock(K, params)
+    blk = evoformer.ShardedBlock(K, params, fp8_trimul=fp8_trimul)
     msa_l, pair_l = msa[blk.shard(n_seq)].to(dev), pair[blk.shard(n_res)].to(dev)
     run = lambda: blk(msa_l, pair_l, msa_mask, pair_mask)
   else:
     msa_l, pair_l = msa.to(dev), pair.to(dev)
-    run = lambda: evoformer.block(K, msa_l, pair_l, msa_mask, pair_mask, params)
+    run = lambda: evoformer.block(K, msa_l, pair_l, msa_mask, pair_mask, params, fp8_trimul=fp8_trimul)
   for _ in range(2):
     run()
   if world > 1:
@@ -182,7 +183,8 @@ def main():
   torch.cuda.set_device(local_rank)
   dev = torch.device("cuda", local_rank)
   if world > 1:
-    os.environ["NCCL_DEBUG"] = "WARN"  # NCCL's version banner goes to stdout and would sit in front of the JSON line
+    # NCCL writes its log, the version banner of the VERSION / WARN levels included, to stdout in front of the JSON line
+    os.environ.pop("NCCL_DEBUG", None)
     dist.init_process_group("nccl", device_id=dev)
   lib = _lib.load()
   bf = torch.bfloat16
@@ -305,6 +307,7 @@ def main():
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
   block_ms = evoformer_block_ms(world, rank, dev) if args.block else None
+  block_f8_ms = evoformer_block_ms(world, rank, dev, fp8_trimul=True) if args.block else None
   status = ops.device_status()
   if rank == 0:
     sampler.stop_flag.set()
@@ -329,7 +332,7 @@ def main():
                    "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
                    "device_status": status,
                    "evoformer_block": None if block_ms is None else {
-                       "ms": block_ms, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
+                       "ms": block_ms, "ms_e4m3_trimul": block_f8_ms, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
                        "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,

@@ -73,7 +73,8 @@ def cuda_kernels():
   return types.SimpleNamespace(
       ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,
       opm_projection=ops.opm_projection, outer_product_mean=ops.outer_product_mean,
-      ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, trimul_epilogue=ops.trimul_epilogue,
+      ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, contract_gathered=ops.contract_gathered,
+      trimul_epilogue=ops.trimul_epilogue,
       transition=transition)
 
 
@@ -108,8 +109,11 @@ def transition(K, x, prm):
   return K.transition(x.reshape(-1, shape[-1]), prm["ln"], prm["w1"], prm["b1"], prm["w2"], prm["b2"]).reshape(shape)
 
 
-def block(K, msa, pair, msa_mask, pair_mask, params):
-  """One Evoformer block on one device.  msa [s, r, c_m], pair [r, r, c_z], msa_mask [s, r], pair_mask [r, r] (0/1)."""
+def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False):
+  """One Evoformer block on one device.  msa [s, r, c_m], pair [r, r, c_z], msa_mask [s, r], pair_mask [r, r] (0/1).
+  fp8_trimul: the triangle-multiplication operands are written and contracted in e4m3 (the reference's opt-in
+  fp8_contraction, fused_ops.py:262-275): half the operand bytes, 1.7x the contraction rate, FP8 tolerance."""
+  f8 = {"fp8": True} if fp8_trimul else {}
   d = params["d_head"]
   mm, pm = msa_mask > 0, pair_mask > 0
   msa = attend(K, msa, params["row_attn"], head_bias(K, pair, params["row_attn"]), mm, False, d)
@@ -121,7 +125,7 @@ def block(K, msa, pair, msa_mask, pair_mask, params):
   for name, incoming in (("tri_out", False), ("tri_in", True)):
     t = params[name]
     l, r = K.ln_gated_dual_proj(pair, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], pair_mask.to(pair.dtype),
-                                transpose=incoming)
+                                transpose=incoming, **f8)
     pair = triangle_update(K, pair, K.contract(r, l) if incoming else K.contract(l, r), t)
   pair = attend(K, pair, params["tri_attn_start"], head_bias(K, pair, params["tri_attn_start"]), pm, False, d)
   bias_end = head_bias(K, pair, params["tri_attn_end"]).transpose(1, 2).contiguous()
@@ -137,9 +141,10 @@ class ShardedBlock:
   Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
   replicated.  s and r must be divisible by the world size."""
 
-  def __init__(self, K, params, group=None):
+  def __init__(self, K, params, group=None, fp8_trimul=False):
     import torch.distributed as dist
     self.K, self.params, self.dist, self.group = K, params, dist, group
+    self.f8 = {"fp8": True} if fp8_trimul else {}  # e4m3 triangle operands: the gathered operand is half the bytes
     self.P = dist.get_world_size(group)
     self.rank = dist.get_rank(group)
 
@@ -164,8 +169,18 @@ class ShardedBlock:
   def gather(self, x, dim):
     x = x.contiguous()
     out = torch.empty((self.P * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
-    self.dist.all_gather_into_tensor(out, x, group=self.group)
+    if x.element_size() == 1:  # e4m3 operands travel as bytes
+      self.dist.all_gather_into_tensor(out.view(torch.uint8), x.view(torch.uint8), group=self.group)
+    else:
+      self.dist.all_gather_into_tensor(out, x, group=self.group)
     return out if dim == 0 else torch.cat(list(out.view((self.P,) + tuple(x.shape)).unbind(0)), dim=dim)
+
+  def contract_all(self, a, b_local):
+    """contract(a, every rank's b_local stacked on the row axis).  The gathered operand is read where the all-gather
+    wrote it ([P, c, rows/P, k]) when its parts are whole 128-row tiles; otherwise it is re-laid out first."""
+    if b_local.shape[1] % 128 == 0:
+      return self.K.contract_gathered(a, self.gather(b_local, 0).view((self.P,) + tuple(b_local.shape)))
+    return self.K.contract(a, self.gather(b_local, 1))
 
   def shard(self, n):
     step = n // self.P
@@ -192,14 +207,14 @@ class ShardedBlock:
     # 5 triangle multiplication, outgoing edges: local rows of the left operand, all rows of the right
     t = prm["tri_out"]
     l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
-                                 pair_mask[rs].contiguous().to(pair_r.dtype))
-    pair_r = triangle_update(K, pair_r, K.contract(l, self.gather(rr, 1)), t)
+                                 pair_mask[rs].contiguous().to(pair_r.dtype), **self.f8)
+    pair_r = triangle_update(K, pair_r, self.contract_all(l, rr), t)
     # 6 incoming edges: operands come from the column-sharded pair, read transposed
     t = prm["tri_in"]
     pair_c = self.rows_to_cols(pair_r)
     l, rr = K.ln_gated_dual_proj(pair_c, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
-                                 pair_mask[:, rs].contiguous().to(pair_r.dtype), transpose=True)
-    pair_r = triangle_update(K, pair_r, K.contract(rr, self.gather(l, 1)), t)
+                                 pair_mask[:, rs].contiguous().to(pair_r.dtype), transpose=True, **self.f8)
+    pair_r = triangle_update(K, pair_r, self.contract_all(rr, l), t)
     # 7 triangle attention, starting node
     bias = self.gather(head_bias(K, pair_r, prm["tri_attn_start"]), 1)
     pair_r = attend(K, pair_r, prm["tri_attn_start"], bias, pm[rs].contiguous(), False, d)

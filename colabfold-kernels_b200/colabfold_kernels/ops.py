@@ -147,6 +147,18 @@ def contract(a, b, alpha=1.0):
   return out
 
 
+def contract_gathered(a, b_parts, alpha=1.0):
+  """contract(a, b) with b given as [parts, c, j/parts, k], an all-gather's output, read in place -> [c, i, j] bf16."""
+  a, b_parts = _c(a), _c(b_parts)
+  c, i, k = a.shape
+  parts, _, jp, _ = b_parts.shape
+  out = torch.empty((c, i, parts * jp), dtype=torch.bfloat16, device=a.device)
+  with torch.cuda.device(a.device):
+    _lib.call("cfk_contract_gathered", _ptr(a), _ptr(b_parts), _ptr(out), c, i, parts * jp, k, tag(a.dtype), float(alpha), parts,
+              _stream())
+  return out
+
+
 # ------------------------------------------------------------------------------------------ projection family
 def _f32(t):
   return _c(t.float())

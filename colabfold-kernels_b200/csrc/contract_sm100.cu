@@ -34,6 +34,7 @@ struct ContractParams {
   float alpha;
   int* status;
   int opm;              // 1: rows are (i, 32 channels), columns (j, 32 channels); the product is stored as [i, j, 32, 32]
+  int part_rows;        // > 0: b is [parts, C, part_rows, K] (an all-gather's output); a multiple of 128
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,7 +95,17 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
           if (!ok) { report_timeout(prm.status, 401); break; }
           mbar_arrive_expect_tx(&full[st], kSliceA + kSliceB);
           tma_load_3d(smem + kOffA + st * kSliceA, &tm_a, &full[st], s * prm.k_per_slice, i0, c);
-          tma_load_3d(smem + kOffB + st * kSliceB, &tm_b, &full[st], s * prm.k_per_slice, j0, c);
+          if (prm.part_rows > 0) {
+            // rows j0 .. j0+255 of the gathered operand: two 128-row boxes, each inside one part
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int j = j0 + h * 128;
+              tma_load_4d(smem + kOffB + st * kSliceB + h * (128 * 128), &tm_b, &full[st], s * prm.k_per_slice,
+                          j % prm.part_rows, c, j / prm.part_rows);
+            }
+          } else {
+            tma_load_3d(smem + kOffB + st * kSliceB, &tm_b, &full[st], s * prm.k_per_slice, j0, c);
+          }
         }
       }
     }
@@ -202,8 +213,9 @@ using namespace cfk;
 
 namespace {
 // opm_ri > 0: a is [(opm_ri x 32), k], b [(opm_rj x 32), k] and the product is stored as out[opm_ri, opm_rj, 32, 32]
+// parts > 1: b is [parts, c, j / parts, k], the layout an all-gather of per-rank [c, j / parts, k] operands leaves
 int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha, int opm_ri,
-                  int opm_rj, void* stream) {
+                  int opm_rj, int parts, void* stream) {
   if (a == nullptr || b == nullptr || out == nullptr) return CFK_ERR_NULL;
   if (c <= 0 || i <= 0 || j <= 0 || k <= 0) return CFK_ERR_SHAPE;
   if (dtype != CFK_BF16 && dtype != CFK_E4M3) return CFK_ERR_DTYPE;
@@ -219,7 +231,17 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
     int rc = make_tensor_map(&ta, a, dtype, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  {
+  int part_rows = 0;
+  if (parts > 1) {
+    if (j % parts != 0 || (j / parts) % 128 != 0) return CFK_ERR_SHAPE;
+    part_rows = j / parts;
+    // a box past the last part (J not a multiple of 256) reads the fill value, as the 3-D map does past J
+    uint64_t dims[4] = {uint64_t(k), uint64_t(part_rows), uint64_t(c), uint64_t(parts)};
+    uint64_t str[3] = {uint64_t(k) * es, uint64_t(part_rows) * k * es, uint64_t(c) * part_rows * k * es};
+    uint32_t box[4] = {uint32_t(128 / es), 128, 1, 1};
+    int rc = make_tensor_map(&tb, b, dtype, 4, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  } else {
     uint64_t dims[3] = {uint64_t(k), uint64_t(j), uint64_t(c)};
     uint64_t str[2] = {uint64_t(k) * es, uint64_t(j) * k * es};
     uint32_t box[3] = {uint32_t(128 / es), kTN, 1};
@@ -241,7 +263,7 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
     int rc = make_tensor_map(&to, out, CFK_BF16, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0};
+  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0, part_rows};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   static bool attr_set = false;
   if (!attr_set) {
@@ -261,10 +283,16 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
 
 extern "C" int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
                             void* stream) {
-  return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, stream);
+  return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, 1, stream);
+}
+
+extern "C" int cfk_contract_gathered(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
+                                     float alpha, int parts, void* stream) {
+  if (parts <= 0) return CFK_ERR_SHAPE;
+  return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, parts, stream);
 }
 
 extern "C" int cfk_opm_outer_product(const void* a, const void* b, void* out, int ri, int rj, int s, int dtype, void* stream) {
   if (ri <= 0 || rj <= 0 || s <= 0) return CFK_ERR_SHAPE;
-  return contract_impl(a, b, out, 1, ri * 32, rj * 32, s, dtype, 1.0f, ri, rj, stream);
+  return contract_impl(a, b, out, 1, ri * 32, rj * 32, s, dtype, 1.0f, ri, rj, 1, stream);
 }

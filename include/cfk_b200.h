@@ -125,6 +125,12 @@ CFK_API int cfk_trim_limits(const uint8_t* kmask, int32_t* limits, int batch, in
 CFK_API int cfk_contract(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha,
                          void* stream);
 
+/* The same contraction with b given as [parts, C, J/parts, K]: what an all-gather over `parts` ranks of per-rank
+ * [C, J/parts, K] right operands leaves in memory, read in place (no re-layout copy).  J/parts must be a multiple
+ * of 128.  The reference runs on one device and has no counterpart; this serves the row-sharded block. */
+CFK_API int cfk_contract_gathered(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
+                                  float alpha, int parts, void* stream);
+
 /* The outer product of the outer-product-mean over the MSA depth, for 32-channel projections:
  * out[i, j, c, e] = sum_s a[i*32 + c, s] * b[j*32 + e, s]; a [ri*32, s], b [rj*32, s] in `dtype` (CFK_BF16 or CFK_E4M3),
  * out [ri, rj, 32, 32] bf16 - the layout the output linear of the module contracts over (c, e) without a transposed

@@ -33,6 +33,9 @@ def oracle_kernels(dtype=torch.float32):
   def contract(a, b):
     return R.ref_contract(a, b, dtype)
 
+  def contract_gathered(a, b_parts):  # b_parts [parts, c, j/parts, k]: the right operand as an all-gather leaves it
+    return R.ref_contract(a, torch.cat(list(b_parts.unbind(0)), dim=1), dtype)
+
   def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, in_scale=None, in_offset=None,
                       eps=1e-5, add_input=False):
     if in_scale is None:
@@ -46,4 +49,4 @@ def oracle_kernels(dtype=torch.float32):
   return types.SimpleNamespace(ln_projection=ln_projection, packed_attention=packed_attention,
                                output_projection=output_projection, opm_projection=opm_projection,
                                outer_product_mean=outer_product_mean, ln_gated_dual_proj=ln_gated_dual_proj,
-                               contract=contract, trimul_epilogue=trimul_epilogue, transition=transition)
+                               contract=contract, contract_gathered=contract_gathered, trimul_epilogue=trimul_epilogue, transition=transition)

@@ -103,3 +103,32 @@ def test_shallow_opm_forms_match_the_reference_fixtures(golden):
   assert fused_ops.opm_outer(cfg, torch.bfloat16, 12, c, d, f) is None       # not 16 rows: the caller's own path
   assert fused_ops.opm_update(cfg, torch.bfloat16, 40, 128) is None           # K not a multiple of 32
   assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("parts,jp,dtype", [(2, 128, "bf16"), (3, 128, "bf16"), (4, 256, "bf16"), (8, 128, "e4m3"),
+                                            (3, 384, "e4m3")])
+def test_contract_reads_an_all_gathered_operand_in_place(parts, jp, dtype):
+  """b as [parts, c, j/parts, k] (what an all-gather of per-rank right operands leaves) gives bit for bit the
+  product of the re-laid-out [c, j, k] operand; part counts that leave j off the 256-row tile included."""
+  from colabfold_kernels import ops
+  c, i, k = 5, 200, 264 if dtype == "bf16" else 272
+  g = torch.Generator().manual_seed(parts * 1000 + jp)
+  dt = torch.bfloat16 if dtype == "bf16" else torch.float8_e4m3fn
+  a = torch.randn(c, i, k, generator=g).to(dt).cuda()
+  b_parts = torch.randn(parts, c, jp, k, generator=g).to(dt).cuda()
+  whole = torch.cat(list(b_parts.unbind(0)), dim=1).contiguous()
+  out = ops.contract_gathered(a, b_parts)
+  ref = ops.contract(a, whole)
+  assert ops.device_status() == 0
+  assert out.shape == (c, i, parts * jp)
+  assert torch.equal(out, ref)
+  # and the reference itself is right (oracle), so the pair cannot be wrong together
+  assert O.rel_err(ref.cpu().float(), O.ref_contract(a.cpu().float(), whole.cpu().float())) <= (8e-3 if dtype == "bf16" else 6e-2)
+
+
+def test_contract_gathered_rejects_parts_that_split_a_tile():
+  from colabfold_kernels import ops
+  a = torch.zeros(1, 128, 64, dtype=torch.bfloat16, device="cuda")
+  b = torch.zeros(2, 1, 64, 64, dtype=torch.bfloat16, device="cuda")
+  with pytest.raises(RuntimeError):
+    ops.contract_gathered(a, b)

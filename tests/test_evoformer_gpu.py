@@ -28,3 +28,22 @@ def test_block_matches_oracle(s, r):
   assert ops.device_status() == 0
   assert O.rel_err(m.cpu().float(), ref_m) <= 5e-2
   assert O.rel_err(p.cpu().float(), ref_p) <= 5e-2
+
+
+def test_block_with_e4m3_triangle_operands():
+  """The opt-in e4m3 triangle multiplication inside the block against the bf16 block: FP8 tolerance (6e-2)."""
+  from colabfold_kernels import evoformer, ops
+  g = torch.Generator().manual_seed(1)
+  bf = torch.bfloat16
+  s, r = 16, 128
+  msa, pair = torch.randn(s, r, 256, generator=g).to(bf).cuda(), torch.randn(r, r, 128, generator=g).to(bf).cuda()
+  msa_mask = (torch.rand(s, r, generator=g) < 0.95).float().cuda()
+  pair_mask = (torch.rand(r, r, generator=g) < 0.95).float().cuda()
+  params = evoformer.init_params(seed=3, device="cuda")
+  K = evoformer.cuda_kernels()
+  m0, p0 = evoformer.block(K, msa, pair, msa_mask, pair_mask, params)
+  m1, p1 = evoformer.block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=True)
+  assert ops.device_status() == 0
+  assert O.rel_err(m1.cpu().float(), m0.cpu().float()) <= 6e-2
+  assert O.rel_err(p1.cpu().float(), p0.cpu().float()) <= 6e-2
+  assert not torch.equal(p0, p1)  # the e4m3 path really ran
