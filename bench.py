@@ -109,7 +109,7 @@ def cpu_arm(steps, warmup, sample_b=32):
                     f"median of {len(times)}", "ms_per_sample": sec * 1e3}
 
 
-def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False):
+def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False, graph=True):
   """Second metric: one Evoformer block (inference wiring of the fused ops) at N_seq=512, N_res=1024, device-timed,
   max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed).  fp8_trimul: the
   reference's opt-in e4m3 triangle contraction (half the bytes of the operand the ranks exchange)."""
@@ -136,6 +136,15 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   if world > 1:
     dist.barrier()
   torch.cuda.synchronize()
+  launch = "eager"
+  if graph:
+    # the block is ~100 short launches: one graph launch keeps the host out of the timed region
+    run, _ = evoformer.capture(run)
+    launch = "cuda graph"
+    run()
+    if world > 1:
+      dist.barrier()
+    torch.cuda.synchronize()
   e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
   e0.record()
   for _ in range(iters):
@@ -145,7 +154,7 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   ms = torch.tensor([e0.elapsed_time(e1) / iters], device=dev)
   if world > 1:
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-  return float(ms)
+  return float(ms), launch
 
 
 def main():
@@ -155,6 +164,7 @@ def main():
   ap.add_argument("--warmup", type=int, default=3)
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
   ap.add_argument("--block", type=int, default=1, help="also time one Evoformer block (0 to skip)")
+  ap.add_argument("--block-graph", type=int, default=1, help="replay the block as one CUDA graph (0: launch op by op)")
   ap.add_argument("--batch", type=int, default=B, help="batch rows per GPU (smaller values are for profiler captures only)")
   args = ap.parse_args()
   globals()["B"] = args.batch
@@ -306,8 +316,11 @@ def main():
   del ref_out, ref_lse, ref_dk
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-  block_ms = evoformer_block_ms(world, rank, dev) if args.block else None
-  block_f8_ms = evoformer_block_ms(world, rank, dev, fp8_trimul=True) if args.block else None
+  block_ms = block_f8_ms = block_launch = None
+  if args.block:
+    graph = args.block_graph != 0
+    block_ms, block_launch = evoformer_block_ms(world, rank, dev, graph=graph)
+    block_f8_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, graph=graph)
   status = ops.device_status()
   if rank == 0:
     sampler.stop_flag.set()
@@ -332,7 +345,7 @@ def main():
                    "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
                    "device_status": status,
                    "evoformer_block": None if block_ms is None else {
-                       "ms": block_ms, "ms_e4m3_trimul": block_f8_ms, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
+                       "ms": block_ms, "ms_e4m3_trimul": block_f8_ms, "launch": block_launch, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
                        "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,

@@ -226,3 +226,21 @@ class ShardedBlock:
     # 9 pair transition
     pair_r = transition(K, pair_r, prm["pair_transition"])
     return msa_s, pair_r
+
+
+def capture(fn):
+  """Record one call of fn() (kernels, copies and NCCL collectives alike) into a CUDA graph on a side stream and
+  return (replay, outputs): replay() launches the whole recorded block with one host call, writing into the same
+  output tensors.  fn must have run before (extension attributes set, communicators built) and its inputs must stay
+  where they are; every rank of a sharded block captures and replays together."""
+  side = torch.cuda.Stream()
+  side.wait_stream(torch.cuda.current_stream())
+  with torch.cuda.stream(side):
+    fn()  # once on the capturing stream: allocator pools and lazy state settle before the recording
+  torch.cuda.current_stream().wait_stream(side)
+  torch.cuda.synchronize()
+  graph = torch.cuda.CUDAGraph()
+  with torch.cuda.graph(graph, stream=side):
+    outputs = fn()
+  return graph.replay, outputs
+

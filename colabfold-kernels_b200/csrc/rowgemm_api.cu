@@ -27,9 +27,10 @@ int run_chunks(RowGemmParams prm, int total_chunks, const void* w0, const void* 
   if (fit < 1) return CFK_ERR_UNSUPPORTED;
   prm.status = device_status_word();
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
-  if (fit < total_chunks && rowgemm_stream_fits(prm)) {
-    // The weights of all chunks do not fit beside the pipeline: rather than one launch per group of chunks (each
-    // reading the activations again from HBM), one launch streams the chunk weights from L2 through a two-slot ring.
+  if ((fit < total_chunks || (total_chunks > 1 && rowgemm_resident_is_tight(prm, total_chunks))) && rowgemm_stream_fits(prm)) {
+    // The weights of all chunks do not fit beside the pipeline, or fit only by squeezing it to one output staging
+    // buffer (every store then waits for its own read): rather than one launch per group of chunks (each reading the
+    // activations again from HBM), one launch streams the chunk weights from L2 through a two-slot ring.
     prm.chunk0 = 0;
     prm.chunks = total_chunks;
     prm.stream_weights = 1;

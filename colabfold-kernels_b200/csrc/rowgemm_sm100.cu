@@ -810,6 +810,18 @@ int rowgemm_chunks_that_fit(const RowGemmParams& p) {
   return fit;
 }
 
+// With `chunks` chunk weights resident, is there no room left for two stages and two output staging buffers while the
+// two-slot weight ring would leave it?
+bool rowgemm_resident_is_tight(const RowGemmParams& p, int chunks) {
+  const int nsrc = p.src[1].x != nullptr ? 2 : 1;
+  const int k0 = p.src[0].k, k1 = nsrc == 2 ? p.src[1].k : k0;
+  const Plan sp = make_plan(p);
+  const int per_chunk = (p.n_chunk / 64) * 128 * (k0 + (p.dual ? k1 : 0));
+  const int fixed = kSmemFixed + (p.keep != nullptr ? kMaxTilesPerCta : 0);
+  const int want = 2 * sp.stage_bytes + 2 * sp.o_bytes;
+  return sp.o_bytes > 0 && kSmemBudget - fixed - chunks * per_chunk < want && kSmemBudget - fixed - 2 * per_chunk >= want;
+}
+
 bool rowgemm_stream_fits(const RowGemmParams& p) {
   const int nsrc = p.src[1].x != nullptr ? 2 : 1;
   const int k0 = p.src[0].k, k1 = nsrc == 2 ? p.src[1].k : k0;

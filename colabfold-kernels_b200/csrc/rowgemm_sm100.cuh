@@ -71,6 +71,7 @@ struct RowGemmParams {
 };
 
 int rowgemm_chunks_that_fit(const RowGemmParams& prm);
+bool rowgemm_resident_is_tight(const RowGemmParams& prm, int chunks);  // resident weights leave < 2 stages + 2 staging buffers
 bool rowgemm_stream_fits(const RowGemmParams& prm);    // room for a two-chunk weight ring, one stage and the staging buffer  // chunks whose weights fit beside two pipeline stages
 int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st);
 int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
