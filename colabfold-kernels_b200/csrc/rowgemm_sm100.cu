@@ -96,7 +96,7 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 8);
+      mbar_init(&acc_empty[i], L.no == 2 ? 4 : 8);  // the epilogue warps that read one accumulator: one group or both
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 1);
       mbar_init(&ws_full[i], 1);
@@ -286,15 +286,7 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     // channel-major source the even or odd 8-channel groups), and the halves combine their LayerNorm statistics by
     // shuffle (pairwise mean / sum of squared deviations).
     // register budgets: 128 x 40 + 256 x (104 + 112) stays inside the 640 x 96 the CTA is launched with
-    if (SRC0 != 0) {
-      if (SRC0 != 0) {
-      asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
-    } else {
-      asm volatile("setmaxnreg.inc.sync.aligned.u32 112;");
-    }
-    } else {
-      asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
-    }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
     const int pt = (warp - 4) * 32 + lane;
     const int trow = pt >> 1, half = pt & 1;
     bool ok = true;
@@ -464,7 +456,11 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
     } else {
       asm volatile("setmaxnreg.inc.sync.aligned.u32 112;");
     }
-    // two groups of four warps share every chunk: group g takes the 32-column pieces g, g + 2
+    // Two groups of four warps.  With two staging buffers they take the chunks in turn (group = accumulator buffer =
+    // staging buffer = chunk parity): while one group waits for its accumulator, its residual or its store, the other
+    // is in its arithmetic.  With one staging buffer (or none) they share every chunk: group g takes the 32-column
+    // pieces g, g + 2.
+    const bool alt = NO == 2;
     const int quad = warp & 3, trow = quad * 32 + lane, grp = (warp - 12) >> 2;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     bool ok = true;
@@ -527,6 +523,8 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
       }
       for (int c = 0; c < p.chunks; ++c, ++cc) {
         const int buf = cc & 1;
+        if (alt && buf != grp) continue;  // the other group's chunk
+        const int sub0 = alt ? 0 : grp, dsub = alt ? 1 : 2;
         const int cg = p.chunk0 + c;
         const int bcol = (cg / p.chunks_per_slot) * p.bias_slot_stride + (cg % p.chunks_per_slot) * p.n_chunk;  // bias index
         const int arr = two_out ? 0 : cg / p.chunks_per_array;
@@ -544,30 +542,36 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           nxt[q] = make_uint4(0, 0, 0, 0);
-          if (rowp != nullptr && ocol + grp * 32 + q * 8 < p.n_valid) nxt[q] = *reinterpret_cast<const uint4*>(rowp + grp * 32 + q * 8);
+          if (rowp != nullptr && ocol + sub0 * 32 + q * 8 < p.n_valid) nxt[q] = *reinterpret_cast<const uint4*>(rowp + sub0 * 32 + q * 8);
         }
         if (ok && !mbar_wait_deadline(&acc_full[buf], (cc >> 1) & 1)) {
           report_timeout(p.status, 905);
           ok = false;
         }
-        if (staged && ok) {
-          // the staging buffer is ours once its residual chunk has landed or, without one, once the store that last
-          // used it has read it
-          const bool landed = ka.resid_tma != 0;
-          if (!mbar_wait_deadline(landed ? &o_full[ob] : &o_empty[ob], landed ? (cc / NO) & 1 : ((cc / NO) & 1) ^ 1)) {
-            report_timeout(p.status, 908);
-            ok = false;
+        const bool landed = ka.resid_tma != 0;
+        if (staged) {
+          // The staging buffer is ours once its residual chunk has landed or, without one, once the store that last
+          // used it has read it: with two buffers that store is this group's own previous one (its issuer waits and
+          // the group meets), with one buffer o_empty says so.
+          if (landed || !alt) {
+            if (ok && !mbar_wait_deadline(landed ? &o_full[ob] : &o_empty[ob], landed ? (cc / NO) & 1 : ((cc / NO) & 1) ^ 1)) {
+              report_timeout(p.status, 908);
+              ok = false;
+            }
+          } else {
+            if (trow == 0) tma_wait_group_read<0>();
+            named_bar_sync(3 + grp, 128);
           }
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int sub = grp; sub < p.n_chunk / 32; sub += 2) {
+        for (int sub = sub0; sub < p.n_chunk / 32; sub += dsub) {
           float y[2][32];
           uint4 add[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             add[q] = nxt[q];
-            const int cq = (sub + 2) * 32 + q * 8;
+            const int cq = (sub + dsub) * 32 + q * 8;
             nxt[q] = make_uint4(0, 0, 0, 0);
             if (rowp != nullptr && cq < p.n_chunk && ocol + cq < p.n_valid) nxt[q] = *reinterpret_cast<const uint4*>(rowp + cq);
           }
@@ -702,8 +706,9 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         if (staged) {
           fence_proxy_async();
-          named_bar_sync(3, 256);
-          if (trow == 0 && grp == 0) {
+          if (alt) named_bar_sync(3 + grp, 128);
+          else named_bar_sync(3, 256);
+          if (trow == 0 && (alt || grp == 0)) {
             if (ok) {
               for (int i = 0; i < nouts; ++i) {
                 const int a_idx = two_out ? i : arr;
@@ -718,18 +723,15 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
               }
             }
             tma_commit_group();
-            if (NO == 1) {
+            if (landed || !alt) {  // o_empty is waited for: by the residual producer, or by both groups (one buffer)
               tma_wait_group_read<0>();
-              mbar_arrive(&o_empty[0]);
-            } else {
-              tma_wait_group_read<1>();
-              if (cc >= 1) mbar_arrive(&o_empty[(cc - 1) & 1]);
+              mbar_arrive(&o_empty[ob]);
             }
           }
         }
       }
     }
-    if (staged && trow == 0 && grp == 0) tma_wait_group<0>();
+    if (staged && trow == 0) tma_wait_group<0>();
   }
   tc_fence_before();
   __syncthreads();

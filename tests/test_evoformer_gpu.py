@@ -47,3 +47,29 @@ def test_block_with_e4m3_triangle_operands():
   assert O.rel_err(m1.cpu().float(), m0.cpu().float()) <= 6e-2
   assert O.rel_err(p1.cpu().float(), p0.cpu().float()) <= 6e-2
   assert not torch.equal(p0, p1)  # the e4m3 path really ran
+
+
+def test_block_replayed_as_a_cuda_graph_matches_the_eager_block():
+  """The whole block recorded once into a CUDA graph: a replay writes the same bits as launching op by op, and
+  follows new input values written into the captured input tensors."""
+  from colabfold_kernels import evoformer, ops
+  g = torch.Generator().manual_seed(2)
+  bf = torch.bfloat16
+  s, r = 16, 64
+  msa, pair = torch.randn(s, r, 256, generator=g).to(bf).cuda(), torch.randn(r, r, 128, generator=g).to(bf).cuda()
+  msa_mask = (torch.rand(s, r, generator=g) < 0.9).float().cuda()
+  pair_mask = (torch.rand(r, r, generator=g) < 0.9).float().cuda()
+  params = evoformer.init_params(seed=4, device="cuda")
+  K = evoformer.cuda_kernels()
+  run = lambda: evoformer.block(K, msa, pair, msa_mask, pair_mask, params)
+  m0, p0 = run()
+  replay, (mg, pg) = evoformer.capture(run)
+  replay()
+  torch.cuda.synchronize()
+  assert torch.equal(mg, m0) and torch.equal(pg, p0)
+  msa.copy_(torch.randn(s, r, 256, generator=g).to(bf))
+  m1, p1 = run()
+  replay()
+  torch.cuda.synchronize()
+  assert ops.device_status() == 0
+  assert torch.equal(mg, m1) and torch.equal(pg, p1) and not torch.equal(m1, m0)
