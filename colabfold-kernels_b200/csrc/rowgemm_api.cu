@@ -152,7 +152,8 @@ extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const flo
   prm.src[0] = row_major(x, a, ln_scale, ln_offset);
   prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.eps = eps;
   prm.mode = kModeLinear; prm.dual = 0;
-  prm.n_chunk = n >= 128 ? 128 : 64;
+  // 256 input channels: 64-column chunks leave room for two stages and two staging buffers beside the weight ring
+  prm.n_chunk = (n >= 128 && a != 256) ? 128 : 64;
   if (n % prm.n_chunk != 0 && g > 1) return CFK_ERR_UNSUPPORTED;
   const int cps = (n + prm.n_chunk - 1) / prm.n_chunk;
   prm.chunks_per_slot = cps; prm.chunks_per_array = g * cps; prm.bias_slot_stride = 0;
@@ -189,7 +190,7 @@ extern "C" int cfk_output_projection(const void* o, const void* w, const void* b
   prm.src[0] = row_major(o, k, nullptr, nullptr);
   prm.outer = 1; prm.inner = m; prm.inner_pad = m;
   prm.mode = kModeLinear; prm.dual = 0;
-  prm.n_chunk = c >= 128 ? 128 : 64;
+  prm.n_chunk = (c >= 128 && k != 256) ? 128 : 64;  // as in cfk_ln_projection
   const int cps = (c + prm.n_chunk - 1) / prm.n_chunk;
   prm.chunks_per_slot = cps; prm.chunks_per_array = cps;
   prm.bias[0] = b; prm.bias_len = c;
