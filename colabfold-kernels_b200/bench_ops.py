@@ -65,7 +65,21 @@ def make_cases(m, n, c=128):
   a2 = rnd(c, n, n).to(bf)
   a8, b8 = a.to(torch.float8_e4m3fn), a2.to(torch.float8_e4m3fn)
   E = 2  # bytes per bf16
+  # triangle attention of the block: 4 heads of 32 over an [n, n] pair, packed q/k/v/gate
+  h, d = 4, 32
+  pk = rnd(n, n, 4, h, d).to(bf)
+  tri_bias = rnd(h, n, n).to(bf)
+  kmask = torch.rand(n, n, device=dev, generator=g) < 0.95
+  gb = rnd(h, d).to(bf)
+  qscale = torch.tensor([d ** -0.5 * 1.4426950408889634, 1.0], device=dev)
+  qk8 = (pk[:, :, :2].float() * qscale[None, None, :, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+  vg = pk[:, :, 2:].contiguous()
+  attn_flops = 4.0 * n * h * n * n * d
+  attn_bytes = 5 * n * n * h * d * E + h * n * n * E + n * n
   return {
+      "packed_attention": (lambda: ops.packed_attention_fwd(pk, tri_bias, kmask, gb, d ** -0.5), attn_bytes, attn_flops),
+      "packed_attention_qk_e4m3": (lambda: ops.packed_attention_fwd(vg, tri_bias, kmask, gb, d ** -0.5, p8=qk8),
+                                   attn_bytes - 2 * n * n * h * d, attn_flops),
       "layer_norm": (lambda: ops.layer_norm(x, ones, zeros), 2 * m * c * E, 0),
       "ln_gated_dual_proj": (lambda: ops.ln_gated_dual_proj(x, ones, zeros, wp, bp, wp, bp, mask), m * c * E + 2 * m * c * E + m * E,
                              2.0 * m * c * 4 * c),
@@ -99,7 +113,7 @@ def main():
     fn, nbytes, flops = cases[name]
     ms = timed(fn, args.iters)
     gbs, tfs = nbytes / ms / 1e6, flops / ms / 1e9
-    tensor_bound = name.startswith("contract")
+    tensor_bound = name.startswith("contract") or name.startswith("packed_attention")
     print(json.dumps({
         "op": name, "rows": args.rows if not tensor_bound else None, "n": args.n if tensor_bound else None, "ms": round(ms, 4),
         "gb_per_s": round(gbs, 1), "tflop_per_s": round(tfs, 1), "bound": "tensor" if tensor_bound else "hbm",

@@ -70,12 +70,23 @@ def _k_ok(k):
 
 
 def fp8_attention(global_config, key_dim):
-  """e4m3 k/v slots for packed attention are not built for this backend (fused_ops.py:75-80)."""
+  """The k/v form of the e4m3 packed attention (fused_ops.py:75-80) is not this backend's: its kernel takes q and k
+  (fp8_attention_slots), as the reference's Mosaic kernel does, so this answers False like there."""
   return False
 
 
+LOG2E = 1.4426950408889634
+
+
 def fp8_attention_slots(global_config, dtype, key_dim, seq_len):
-  return None
+  """(f8_slots, f8_scales) for the projection to write in e4m3 for packed_attention, or None (fused_ops.py:83-97):
+  asked for by global_config.fp8 at the head dim the tensor-core kernel serves (32: one K = 32 step of the 8-bit
+  MMA).  q (slot 0) is rounded after its static scale sm_scale * log2(e), k (slot 1) as it is."""
+  if not global_config.get("fp8", False) or key_dim != 32:
+    return None
+  if dtype is not None and _norm_dtype(dtype) != torch.bfloat16:
+    return None
+  return (0, 1), (key_dim ** -0.5 * LOG2E, 1.0)
 
 
 def half_attention(global_config):
@@ -88,8 +99,14 @@ def packed_attention(global_config, dtype, key_dim, value_dim):
   (fused_ops.py:152-178).  global_config.trim_padding selects the trim semantics."""
   if attention(global_config, dtype, key_dim, value_dim) is None or key_dim != value_dim:
     return None
-  from colabfold_kernels import grads
-  return functools.partial(grads.packed_attention, trim=bool(global_config.get("trim_padding", False)))
+  from colabfold_kernels import grads, ops
+  trim = bool(global_config.get("trim_padding", False))
+
+  def call(p, bias, kmask, gate_bias=None, p8=None, *, sm_scale, column=False):
+    if p8 is not None:  # the e4m3 q.k form is forward only, like the reference's (fused_ops.py:122-136)
+      return ops.packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=column, trim=trim, p8=p8)
+    return grads.packed_attention(p, bias, kmask, gate_bias, sm_scale=sm_scale, column=column, trim=trim)
+  return call
 
 
 def gated_dual_proj(global_config, dtype, activation=None):
@@ -172,7 +189,13 @@ def ln_projection(global_config, dtype, num_channel, num_output=None):
 
   def fwd(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5):
     return ops.ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps, keep=keep)
-  return grads.differentiable_via(fwd, reference.ref_ln_projection, nondiff=("eps",))
+  diff = grads.differentiable_via(fwd, reference.ref_ln_projection, nondiff=("eps",))
+
+  def call(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5, f8_slots=(), f8_scales=None):
+    if f8_slots:  # -> (p, bias, p8): the e4m3 slots feed the forward-only FP8 attention
+      return ops.ln_projection(x, ln_scale, ln_offset, w, wb, eps=eps, keep=keep, f8_slots=f8_slots, f8_scales=f8_scales)
+    return diff(x, ln_scale, ln_offset, w, wb, keep, eps=eps)
+  return call
 
 
 def output_projection(global_config, dtype, num_input, num_output):

@@ -118,9 +118,13 @@ def trim_limits(kmask):
   return lim
 
 
-def packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=False, trim=False, want_lse=False):
-  """p [X,Y,G,H,D] -> out [X,Y,H,D] (, lse [batch,H,S])."""
+def packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=False, trim=False, want_lse=False, p8=None):
+  """p [X,Y,G,H,D] -> out [X,Y,H,D] (, lse [batch,H,S]).
+  p8 [X,Y,2,H,D] float8_e4m3fn: q (multiplied by sm_scale * log2(e) before rounding, the static scale
+  fp8_attention_slots names) and k; p then holds the remaining slots v[, gate] and the scores run in e4m3."""
   p = _c(p)
+  if p8 is not None:
+    return _packed_attention_qk8(p, _c(p8), bias, kmask, gate_bias, column, trim, want_lse)
   x, y, g, h, d = p.shape
   nb, s = (y, x) if column else (x, y)
   bias = None if bias is None else _c(bias.to(p.dtype))
@@ -132,6 +136,24 @@ def packed_attention_fwd(p, bias, kmask, gate_bias, sm_scale, column=False, trim
   with torch.cuda.device(p.device):
     _lib.call("cfk_packed_attention_fwd", _ptr(p), _ptr(bias), _ptr(km), _ptr(gb), _ptr(out), _ptr(lse), _ptr(lim),
               x, y, g, h, d, tag(p.dtype), int(column), float(sm_scale), _stream())
+  return (out, lse) if want_lse else out
+
+
+def _packed_attention_qk8(p, p8, bias, kmask, gate_bias, column, trim, want_lse):
+  x, y, g, h, d = p.shape
+  if p8.dtype != torch.float8_e4m3fn or tuple(p8.shape) != (x, y, 2, h, d) or p.dtype != torch.bfloat16:
+    raise ValueError("p8 must be float8_e4m3fn [X,Y,2,H,D] beside a bfloat16 p [X,Y,G,H,D]")
+  nb, s = (y, x) if column else (x, y)
+  bias = None if bias is None else _c(bias.to(p.dtype))
+  gb = None if gate_bias is None else _c(gate_bias.to(p.dtype))
+  km = _c(kmask.to(torch.uint8))
+  out = torch.empty((x, y, h, d), dtype=p.dtype, device=p.device)
+  lse = torch.empty((nb, h, s), dtype=torch.float32, device=p.device) if want_lse else None
+  lim = trim_limits(km) if trim else None
+  with torch.cuda.device(p.device):
+    # q carries sm_scale * log2(e): the raw products are log2-domain logits, ln 2 brings them to the natural domain
+    _lib.call("cfk_packed_attention_fwd_qk8", _ptr(p), _ptr(p8), _ptr(bias), _ptr(km), _ptr(gb), _ptr(out), _ptr(lse),
+              _ptr(lim), x, y, g, h, d, int(column), float(0.6931471805599453), _stream())
   return (out, lse) if want_lse else out
 
 
@@ -232,13 +254,25 @@ def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=Non
   return out
 
 
-def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f8_scale=1.0, keep=None):
-  """-> (p [m, g*n] or None, bias [h, m] or None)."""
+def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f8_scale=1.0, keep=None, f8_slots=(),
+                  f8_scales=None):
+  """-> (p [m, g*n] or None, bias [h, m] or None).
+  f8_slots: those slots of w go, each times its static f8_scales entry, to a third output [m, len(f8_slots)*n] in
+  e4m3 (saturating) and p keeps the others: -> (p, bias, p8), as packed_attn.py:234-305 returns them."""
   x = _c(x)
   dt = x.dtype
   m, a = x.shape
   p_out = b_out = None
   kp, kt = _keep(keep)
+  if f8_slots:
+    f8_slots = tuple(f8_slots)
+    scales = tuple(f8_scales) if f8_scales else (1.0,) * len(f8_slots)
+    rest = [g for g in range(w.shape[0]) if g not in f8_slots]
+    # the static scale of a slot is folded into its weights (constants of the model), the kernel rounds with scale 1
+    w8 = torch.stack([w[g].float() * sc for g, sc in zip(f8_slots, scales)]).to(dt)
+    p8, _ = ln_projection(x, ln_scale, ln_offset, w8, None, eps=eps, f8=True, keep=keep)
+    p_rest, b_out = ln_projection(x, ln_scale, ln_offset, w[rest] if rest else None, wb, eps=eps, keep=keep)
+    return p_rest, b_out, p8
   with torch.cuda.device(x.device):
     if w is not None:
       g, _, n = w.shape

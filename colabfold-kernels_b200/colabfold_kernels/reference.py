@@ -64,14 +64,20 @@ def ref_contract(a, b):
   return torch.einsum("cik,cjk->cij", _f(a), _f(b))
 
 
-def ref_ln_projection(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5, **_):
-  """packed_attn.py:308-318 (bf16 slots only)."""
+def ref_ln_projection(x, ln_scale, ln_offset, w=None, wb=None, keep=None, *, eps=1e-5, f8_slots=(), f8_scales=None, **_):
+  """packed_attn.py:308-318: with f8_slots the third output holds those slots times their static scales (fp32 here,
+  before any rounding) and p the others."""
   y = ref_ln(_f(x), _f(ln_scale), _f(ln_offset), eps)
   b = None if wb is None else (y @ _f(wb)).T
   if w is None:
     return None, b
-  p = torch.einsum("ma,gan->mgn", y, _f(w)).reshape(x.shape[0], -1)
-  return p, b
+  p = torch.einsum("ma,gan->mgn", y, _f(w))
+  if not f8_slots:
+    return p.reshape(x.shape[0], -1), b
+  rest = [g for g in range(w.shape[0]) if g not in f8_slots]
+  scales = torch.tensor(list(f8_scales or (1.0,) * len(f8_slots)), dtype=p.dtype)
+  flat = lambda t: t.reshape(x.shape[0], -1)
+  return flat(p[:, rest]), b, flat(p[:, list(f8_slots)] * scales[None, :, None])
 
 
 def ref_output_projection(o, w, b, residual=None, keep=None):

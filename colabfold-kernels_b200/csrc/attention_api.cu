@@ -62,6 +62,32 @@ extern "C" int cfk_packed_attention_fwd(const void* pk, const void* bias, const 
   return attention_fwd_simt(p, dtype, st);
 }
 
+extern "C" int cfk_packed_attention_fwd_qk8(const void* pk, const void* qk8, const void* bias, const uint8_t* kmask,
+                                            const void* gate_bias, void* out, float* lse, const int32_t* trim_limits,
+                                            int x, int y, int g, int h, int d, int column, float scale, void* stream) {
+  if (pk == nullptr || qk8 == nullptr || kmask == nullptr || out == nullptr) return CFK_ERR_NULL;
+  if (x <= 0 || y <= 0 || h <= 0 || d <= 0 || (g != 1 && g != 2)) return CFK_ERR_SHAPE;
+  if ((g == 2) != (gate_bias != nullptr)) return CFK_ERR_NULL;
+  const int64_t slot = int64_t(h) * d, pos = int64_t(g) * slot, pos8 = 2 * slot;
+  AttnProblem p{};
+  const char* base = static_cast<const char*>(pk);
+  const char* base8 = static_cast<const char*>(qk8);
+  p.q = base8; p.k = base8 + slot;          // one byte per element
+  p.v = base; p.gate = g == 2 ? base + slot * 2 : nullptr;
+  p.gate_bias = gate_bias; p.bias = bias; p.kmask = kmask; p.out = out; p.lse = lse; p.trim = trim_limits;
+  const Strides in = column ? Strides{pos, int64_t(y) * pos, d} : Strides{int64_t(y) * pos, pos, d};
+  const Strides in8 = column ? Strides{pos8, int64_t(y) * pos8, d} : Strides{int64_t(y) * pos8, pos8, d};
+  const Strides outs = column ? Strides{slot, int64_t(y) * slot, d} : Strides{int64_t(y) * slot, slot, d};
+  p.sq_ = p.sk_ = in8;
+  p.sv_ = p.sg_ = in;
+  p.so_ = outs;
+  p.nb = column ? y : x; p.h = h; p.sq = p.sk = column ? x : y; p.d = d; p.scale = scale;
+  p.qk_e4m3 = 1;
+  // no second path: the e4m3 scores exist only on the tensor-core kernel
+  if (!attention_sm100_supported(p, CFK_BF16)) return CFK_ERR_UNSUPPORTED;
+  return attention_fwd_sm100(p, static_cast<cudaStream_t>(stream));
+}
+
 namespace cfk {
 namespace {
 // one warp per batch row: the last live key, then (block 0 after a grid-wide atomicMax) the global limit

@@ -22,18 +22,23 @@ namespace cfk {
 
 namespace {
 
-template <int D>
+// F8: q and k arrive in e4m3 (the scores run on the f8f6f4 MMA path, one K = 32 step per 32 head channels); v, P and
+// the output stay bf16.
+template <int D, int F8>
 struct FwdCfg {
   static constexpr int G = 128 / D;  // batch rows per CTA: their O accumulators fill 128 TMEM columns
   static constexpr int kStages = 4;  // K ring and V ring depth
-  static constexpr int kRowBytes = D * 2;
-  static constexpr int kTileQkv = kBQ * kRowBytes;
+  static constexpr int kRowBytes = D * 2;                 // v rows
+  static constexpr int kTileV = kBQ * kRowBytes;
+  static constexpr int kRowBytesQK = D * (F8 ? 1 : 2);    // q and k rows
+  static constexpr int kTileQK = kBQ * kRowBytesQK;
   static constexpr int kTileBias = kBQ * kBK * 2;  // two 64-key halves, 128-byte swizzled rows
   static constexpr int kMaskSlots = 4;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + G * kTileQkv;
-  static constexpr int kOffV = kOffK + kStages * kTileQkv;
-  static constexpr int kOffBias = kOffV + kStages * kTileQkv;
+  static constexpr int kOffK = kOffQ + G * kTileQK;
+  static constexpr int kOffV = kOffK + kStages * kTileQK;
+  static constexpr int kOffBias = kOffV + kStages * kTileV;
+  static_assert(kOffV % 1024 == 0 && kOffBias % 1024 == 0, "swizzled tiles start on their atom");
   static constexpr int kOffMask = kOffBias + 2 * kTileBias;         // float [kMaskSlots][128] additive key mask
   static constexpr int kOffFlag = kOffMask + kMaskSlots * 128 * 4;  // int [kMaskSlots]: any key masked / past Sk
   static constexpr int kOffState = kOffFlag + 16;                   // float [2][G][128]: reference max, row sum
@@ -56,12 +61,12 @@ struct FwdParams {
   int has_bias;
 };
 
-template <int D>
+template <int D, int F8>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_bias,
                       const FwdParams prm) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, F8>;
   constexpr int G = C::G;
   constexpr int ST = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -143,8 +148,8 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (lane == 0) {
         bool ok = true;
         for (int g = 0; g < gcount; ++g) {
-          mbar_arrive_expect_tx(&q_full[g], C::kTileQkv);
-          tma_load_4d(smem + C::kOffQ + g * C::kTileQkv, &tm_q, &q_full[g], 0, q0, head, b0 + g);
+          mbar_arrive_expect_tx(&q_full[g], C::kTileQK);
+          tma_load_4d(smem + C::kOffQ + g * C::kTileQK, &tm_q, &q_full[g], 0, q0, head, b0 + g);
         }
         int step = 0;
         for (int j = 0; j < nj && ok; ++j) {
@@ -161,8 +166,8 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             const int st = step % ST;
             ok = mbar_wait_deadline(&k_empty[st], ((step / ST) & 1) ^ 1);
             if (!ok) { report_timeout(prm.status, 102); break; }
-            mbar_arrive_expect_tx(&k_full[st], C::kTileQkv);
-            tma_load_4d(smem + C::kOffK + st * C::kTileQkv, &tm_k, &k_full[st], 0, j * kBK, head, b0 + g);
+            mbar_arrive_expect_tx(&k_full[st], C::kTileQK);
+            tma_load_4d(smem + C::kOffK + st * C::kTileQK, &tm_k, &k_full[st], 0, j * kBK, head, b0 + g);
           }
         }
       }
@@ -173,19 +178,19 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         for (int step = 0; step < nsteps; ++step) {
           const int st = step % ST, g = step % gcount, j = step / gcount;
           if (!mbar_wait_deadline(&v_empty[st], ((step / ST) & 1) ^ 1)) { report_timeout(prm.status, 103); break; }
-          mbar_arrive_expect_tx(&v_full[st], C::kTileQkv);
-          tma_load_4d(smem + C::kOffV + st * C::kTileQkv, &tm_v, &v_full[st], 0, j * kBK, head, b0 + g);
+          mbar_arrive_expect_tx(&v_full[st], C::kTileV);
+          tma_load_4d(smem + C::kOffV + st * C::kTileV, &tm_v, &v_full[st], 0, j * kBK, head, b0 + g);
         }
       }
       __syncwarp();
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        constexpr uint32_t idesc_s = make_idesc(kBQ, kBK, 1, 1, 0, 0);
+        constexpr uint32_t idesc_s = F8 ? make_idesc(kBQ, kBK, 0, 0, 0, 0) : make_idesc(kBQ, kBK, 1, 1, 0, 0);
         constexpr uint32_t idesc_pv = make_idesc(kBQ, D, 1, 1, 0, 1);
-        constexpr uint32_t kTile16 = C::kTileQkv >> 4;
-        const uint64_t q_desc0 = desc_k_major(smem_u32(smem + C::kOffQ), C::kRowBytes);
-        const uint64_t k_desc0 = desc_k_major(smem_u32(smem + C::kOffK), C::kRowBytes);
+        constexpr uint32_t kTile16 = C::kTileQK >> 4, kTile16V = C::kTileV >> 4;
+        const uint64_t q_desc0 = desc_k_major(smem_u32(smem + C::kOffQ), C::kRowBytesQK);
+        const uint64_t k_desc0 = desc_k_major(smem_u32(smem + C::kOffK), C::kRowBytesQK);
         const uint64_t v_desc0 = desc_mn_major(smem_u32(smem + C::kOffV), C::kRowBytes, 0);
         // Scalar state advanced by increments only: one lane runs this, and every division or re-derivation
         // here would sit between two MMAs.
@@ -202,7 +207,10 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           const uint64_t a = q_desc0 + uint64_t(s_g * kTile16), b = k_desc0 + uint64_t(s_st * kTile16);
           const uint32_t d = tmem + C::kColS + buf * kBK;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
+          for (int kk = 0; kk < D / (F8 ? 32 : 16); ++kk) {  // 32 bytes of the row per MMA either way
+            if (F8) mma_f8_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
+            else mma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
+          }
           mma_commit(&k_empty[s_st]);
           mma_commit(&s_full[buf]);
           if (buf) se_par1 ^= 1; else se_par0 ^= 1;
@@ -215,7 +223,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (!mbar_wait_deadline(&v_full[p_st], v_par)) { report_timeout(prm.status, 204); return false; }
           if (!mbar_wait_deadline(&p_full[buf], buf ? pf_par1 : pf_par0)) { report_timeout(prm.status, 205); return false; }
           tc_fence_after();
-          const uint64_t b = v_desc0 + uint64_t(p_st * kTile16);
+          const uint64_t b = v_desc0 + uint64_t(p_st * kTile16V);
           const uint32_t d = tmem + C::kColO + p_g * D, a = tmem + C::kColP + buf * (kBK / 2);
           const uint32_t acc0 = p_first ^ 1;  // key block 0 overwrites the accumulator
 #pragma unroll
@@ -472,12 +480,13 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   }
 }
 
-template <int D>
+template <int D, int F8>
 int launch(const AttnProblem& p, cudaStream_t st) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, F8>;
   CUtensorMap tq, tk, tv, tb;
-  int rc = make_qkv_map(&tq, p.q, p.sq_, p.nb, p.h, p.sq, D, kBQ);
-  if (rc == CFK_OK) rc = make_qkv_map(&tk, p.k, p.sk_, p.nb, p.h, p.sk, D, kBK);
+  const int qk_dtype = F8 ? CFK_E4M3 : CFK_BF16;
+  int rc = make_qkv_map(&tq, p.q, p.sq_, p.nb, p.h, p.sq, D, kBQ, qk_dtype);
+  if (rc == CFK_OK) rc = make_qkv_map(&tk, p.k, p.sk_, p.nb, p.h, p.sk, D, kBK, qk_dtype);
   if (rc == CFK_OK) rc = make_qkv_map(&tv, p.v, p.sv_, p.nb, p.h, p.sk, D, kBK);
   if (rc != CFK_OK) return rc;
   if (p.bias != nullptr) {
@@ -492,10 +501,10 @@ int launch(const AttnProblem& p, cudaStream_t st) {
   FwdParams prm{p, device_status_word(), p.bias != nullptr};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   const int smem = C::kSmemBytes + 1024;
-  if (cudaFuncSetAttribute(attn_fwd_sm100_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(attn_fwd_sm100_kernel<D, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return CFK_ERR_LAUNCH;
   dim3 grid((p.nb + C::G - 1) / C::G, (p.sq + kBQ - 1) / kBQ, p.h);
-  attn_fwd_sm100_kernel<D><<<grid, kThreads, smem, st>>>(tq, tk, tv, tb, prm);
+  attn_fwd_sm100_kernel<D, F8><<<grid, kThreads, smem, st>>>(tq, tk, tv, tb, prm);
   return check_launch();
 }
 
@@ -510,12 +519,14 @@ bool attention_sm100_supported(const AttnProblem& p, int dtype) {
     return false;
   if (reinterpret_cast<uintptr_t>(p.kmask) % 4 != 0) return false;
   auto st8 = [](const Strides& s) { return s.b % 8 == 0 && s.s % 8 == 0 && s.h % 8 == 0; };
-  return st8(p.sq_) && st8(p.sk_) && st8(p.sv_) && st8(p.so_) && (p.gate == nullptr || st8(p.sg_));
+  auto st16 = [](const Strides& s) { return s.b % 16 == 0 && s.s % 16 == 0 && s.h % 16 == 0; };  // one-byte elements
+  if (p.qk_e4m3 ? !(st16(p.sq_) && st16(p.sk_)) : !(st8(p.sq_) && st8(p.sk_))) return false;
+  return st8(p.sv_) && st8(p.so_) && (p.gate == nullptr || st8(p.sg_));
 }
 
 int attention_fwd_sm100(const AttnProblem& p, cudaStream_t st) {
   switch (p.d) {
-    case 32: return launch<32>(p, st);
+    case 32: return p.qk_e4m3 ? launch<32, 1>(p, st) : launch<32, 0>(p, st);
     default: return CFK_ERR_UNSUPPORTED;
   }
 }

@@ -24,6 +24,7 @@ struct AttnProblem {
   Strides sq_, sk_, sv_, sg_, so_;
   int nb, h, sq, sk, d;
   float scale;
+  int qk_e4m3;            // q and k are float8 e4m3 (strides in elements of that type); v, gate and out stay bf16
 };
 
 struct AttnBwdProblem {

@@ -112,6 +112,17 @@ CFK_API int cfk_packed_attention_fwd(const void* p, const void* bias, const uint
                              float* lse, const int32_t* trim_limits, int x, int y, int g, int h, int d, int dtype,
                              int column, float scale, void* stream);
 
+/* The opt-in FP8 form of the packed attention: q and k come in e4m3 from qk8 [X,Y,2,H,D] (q already multiplied by its
+ * static scale before rounding, as ln_projection's f8_slots / f8_scales write it, packed_attn.py:214-216), and the
+ * scores run on the 8-bit tensor-core path; p [X,Y,G,H,D] in bf16 keeps the other slots: v (G == 1) or v, gate
+ * (G == 2).  `scale` multiplies the raw q8.k8 products (sm_scale divided by q's static scale: ln 2 for the
+ * sm_scale * log2(e) the reference uses).  P.V, the softmax and the output stay as in cfk_packed_attention_fwd.
+ * Head dim 32 only; CFK_ERR_UNSUPPORTED otherwise (the selector then returns no FP8 slots).
+ * Replaces the e4m3 q.k form of packed_attention (fused_ops.py:83-97,122-136; Mosaic kernel mgpu_attn.py:57). */
+CFK_API int cfk_packed_attention_fwd_qk8(const void* p, const void* qk8, const void* bias, const uint8_t* kmask,
+                                         const void* gate_bias, void* out, float* lse, const int32_t* trim_limits,
+                                         int x, int y, int g, int h, int d, int column, float scale, void* stream);
+
 /* limits[b] = 1 + index of the last live key of batch row b (0 when none), limits[batch] = their maximum:
  * trim_limits(kmask, 1) of packed_attn.py:123-129, concatenated as volta.py:212-213 passes them. */
 CFK_API int cfk_trim_limits(const uint8_t* kmask, int32_t* limits, int batch, int s, void* stream);
