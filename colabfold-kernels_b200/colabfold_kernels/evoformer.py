@@ -86,10 +86,18 @@ def head_bias(K, x, prm):
   return bias.reshape(-1, a, b)
 
 
-def attend(K, x, prm, bias, kmask, column, d_head):
-  """Gated self-attention along axis 1 (rows) or axis 0 (columns) of x [X, Y, c] with residual update."""
+def attend(K, x, prm, bias, kmask, column, d_head, fp8=False):
+  """Gated self-attention along axis 1 (rows) or axis 0 (columns) of x [X, Y, c] with residual update.
+  fp8: the projection writes q (times sm_scale * log2 e) and k in e4m3 and the scores run on the 8-bit tensor-core
+  path (the reference's opt-in, fused_ops.py:83-97); v, the gate and the output stay bf16."""
   X, Y, c = x.shape
   h = prm["heads"]
+  if fp8:
+    scales = (d_head ** -0.5 * 1.4426950408889634, 1.0)
+    p, _, p8 = K.ln_projection(x.reshape(X * Y, c), prm["ln"][0], prm["ln"][1], prm["w"], None, f8_slots=(0, 1), f8_scales=scales)
+    o = K.packed_attention(p.reshape(X, Y, 2, h, d_head), bias, kmask, prm["gate_bias"], d_head ** -0.5, column=column,
+                           p8=p8.reshape(X, Y, 2, h, d_head))
+    return K.output_projection(o.reshape(X * Y, h * d_head), prm["wo"], prm["bo"], x.reshape(X * Y, c)).reshape(X, Y, c)
   p, _ = K.ln_projection(x.reshape(X * Y, c), prm["ln"][0], prm["ln"][1], prm["w"], None)
   o = K.packed_attention(p.reshape(X, Y, 4, h, d_head), bias, kmask, prm["gate_bias"], d_head ** -0.5, column=column)
   return K.output_projection(o.reshape(X * Y, h * d_head), prm["wo"], prm["bo"], x.reshape(X * Y, c)).reshape(X, Y, c)
@@ -109,15 +117,16 @@ def transition(K, x, prm):
   return K.transition(x.reshape(-1, shape[-1]), prm["ln"], prm["w1"], prm["b1"], prm["w2"], prm["b2"]).reshape(shape)
 
 
-def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False):
+def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_attention=False):
   """One Evoformer block on one device.  msa [s, r, c_m], pair [r, r, c_z], msa_mask [s, r], pair_mask [r, r] (0/1).
   fp8_trimul: the triangle-multiplication operands are written and contracted in e4m3 (the reference's opt-in
   fp8_contraction, fused_ops.py:262-275): half the operand bytes, 1.7x the contraction rate, FP8 tolerance."""
   f8 = {"fp8": True} if fp8_trimul else {}
+  fa = {"fp8": True} if fp8_attention else {}  # e4m3 q and k in the four attentions (forward only)
   d = params["d_head"]
   mm, pm = msa_mask > 0, pair_mask > 0
-  msa = attend(K, msa, params["row_attn"], head_bias(K, pair, params["row_attn"]), mm, False, d)
-  msa = attend(K, msa, params["col_attn"], None, mm.t().contiguous(), True, d)
+  msa = attend(K, msa, params["row_attn"], head_bias(K, pair, params["row_attn"]), mm, False, d, **fa)
+  msa = attend(K, msa, params["col_attn"], None, mm.t().contiguous(), True, d, **fa)
   msa = transition(K, msa, params["msa_transition"])
   o = params["opm"]
   left, right = K.opm_projection(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
@@ -127,9 +136,9 @@ def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False):
     l, r = K.ln_gated_dual_proj(pair, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], pair_mask.to(pair.dtype),
                                 transpose=incoming, **f8)
     pair = triangle_update(K, pair, K.contract(r, l) if incoming else K.contract(l, r), t)
-  pair = attend(K, pair, params["tri_attn_start"], head_bias(K, pair, params["tri_attn_start"]), pm, False, d)
+  pair = attend(K, pair, params["tri_attn_start"], head_bias(K, pair, params["tri_attn_start"]), pm, False, d, **fa)
   bias_end = head_bias(K, pair, params["tri_attn_end"]).transpose(1, 2).contiguous()
-  pair = attend(K, pair, params["tri_attn_end"], bias_end, pm.t().contiguous(), True, d)
+  pair = attend(K, pair, params["tri_attn_end"], bias_end, pm.t().contiguous(), True, d, **fa)
   pair = transition(K, pair, params["pair_transition"])
   return msa, pair
 
@@ -141,10 +150,11 @@ class ShardedBlock:
   Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
   replicated.  s and r must be divisible by the world size."""
 
-  def __init__(self, K, params, group=None, fp8_trimul=False):
+  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False):
     import torch.distributed as dist
     self.K, self.params, self.dist, self.group = K, params, dist, group
     self.f8 = {"fp8": True} if fp8_trimul else {}  # e4m3 triangle operands: the gathered operand is half the bytes
+    self.fa = {"fp8": True} if fp8_attention else {}  # e4m3 q and k in the attentions
     self.P = dist.get_world_size(group)
     self.rank = dist.get_rank(group)
 
@@ -193,10 +203,10 @@ class ShardedBlock:
     mm, pm = msa_mask > 0, pair_mask > 0
     # 1 MSA row attention: sequences are independent; the pair bias is assembled from every rank's rows
     bias = self.gather(head_bias(K, pair_r, prm["row_attn"]), 1)
-    msa_s = attend(K, msa_s, prm["row_attn"], bias, mm[ss].contiguous(), False, d)
+    msa_s = attend(K, msa_s, prm["row_attn"], bias, mm[ss].contiguous(), False, d, **self.fa)
     # 2-3 column attention and transition on the residue-sharded MSA
     msa_c = self.rows_to_cols(msa_s)
-    msa_c = attend(K, msa_c, prm["col_attn"], None, mm.t()[rs].contiguous(), True, d)
+    msa_c = attend(K, msa_c, prm["col_attn"], None, mm.t()[rs].contiguous(), True, d, **self.fa)
     msa_c = transition(K, msa_c, prm["msa_transition"])
     # 4 outer product mean: local left projection against everyone's right projection -> local pair rows
     o = prm["opm"]
@@ -217,11 +227,11 @@ class ShardedBlock:
     pair_r = triangle_update(K, pair_r, self.contract_all(rr, l), t)
     # 7 triangle attention, starting node
     bias = self.gather(head_bias(K, pair_r, prm["tri_attn_start"]), 1)
-    pair_r = attend(K, pair_r, prm["tri_attn_start"], bias, pm[rs].contiguous(), False, d)
+    pair_r = attend(K, pair_r, prm["tri_attn_start"], bias, pm[rs].contiguous(), False, d, **self.fa)
     # 8 ending node on the column-sharded pair
     pair_c = self.rows_to_cols(pair_r)
     bias_end = self.gather(head_bias(K, pair_c, prm["tri_attn_end"]), 2).transpose(1, 2).contiguous()
-    pair_c = attend(K, pair_c, prm["tri_attn_end"], bias_end, pm.t()[rs].contiguous(), True, d)
+    pair_c = attend(K, pair_c, prm["tri_attn_end"], bias_end, pm.t()[rs].contiguous(), True, d, **self.fa)
     pair_r = self.cols_to_rows(pair_c)
     # 9 pair transition
     pair_r = transition(K, pair_r, prm["pair_transition"])

@@ -271,7 +271,8 @@ def ln_projection(x, ln_scale, ln_offset, w=None, wb=None, eps=1e-5, f8=False, f
     # the static scale of a slot is folded into its weights (constants of the model), the kernel rounds with scale 1
     w8 = torch.stack([w[g].float() * sc for g, sc in zip(f8_slots, scales)]).to(dt)
     p8, _ = ln_projection(x, ln_scale, ln_offset, w8, None, eps=eps, f8=True, keep=keep)
-    p_rest, b_out = ln_projection(x, ln_scale, ln_offset, w[rest] if rest else None, wb, eps=eps, keep=keep)
+    w_rest = torch.stack([w[g] for g in rest]) if rest else None  # views and a device copy: no host index tensor
+    p_rest, b_out = ln_projection(x, ln_scale, ln_offset, w_rest, wb, eps=eps, keep=keep)
     return p_rest, b_out, p8
   with torch.cuda.device(x.device):
     if w is not None:

@@ -684,11 +684,25 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
             } else if (valid) {
               if (E4M3) {
                 uint8_t* dst = static_cast<uint8_t*>(p.out[a_idx]) + out_row * p.ldo + col;
+                auto two = [&](int j) {
+                  return uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(y[i][j] * p.out_scale, y[i][j + 1] * p.out_scale),
+                                                           __NV_SATFINITE, __NV_E4M3));
+                };
+                // 16 values per 16-byte store when the row allows it (pitch and column count in whole 16-byte pieces)
+                const bool wide = (p.ldo % 16 == 0) && (p.n_valid % 16 == 0) && (reinterpret_cast<uintptr_t>(p.out[a_idx]) % 16 == 0);
 #pragma unroll
-                for (int j = 0; j < 32; j += 2)
-                  if (col + j < p.n_valid)
-                    *reinterpret_cast<uint16_t*>(dst + j) = uint16_t(__nv_cvt_float2_to_fp8x2(
-                        make_float2(y[i][j] * p.out_scale, y[i][j + 1] * p.out_scale), __NV_SATFINITE, __NV_E4M3));
+                for (int j = 0; j < 32; j += 16) {
+                  if (wide) {
+                    if (col + j < p.n_valid)
+                      *reinterpret_cast<uint4*>(dst + j) =
+                          make_uint4(two(j) | (two(j + 2) << 16), two(j + 4) | (two(j + 6) << 16), two(j + 8) | (two(j + 10) << 16),
+                                     two(j + 12) | (two(j + 14) << 16));
+                  } else {
+#pragma unroll
+                    for (int jj = j; jj < j + 16; jj += 2)
+                      if (col + jj < p.n_valid) *reinterpret_cast<uint16_t*>(dst + jj) = uint16_t(two(jj));
+                  }
+                }
               } else {
                 __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out[a_idx]) + out_row * p.ldo + col;
 #pragma unroll

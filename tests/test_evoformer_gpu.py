@@ -73,3 +73,23 @@ def test_block_replayed_as_a_cuda_graph_matches_the_eager_block():
   torch.cuda.synchronize()
   assert ops.device_status() == 0
   assert torch.equal(mg, m1) and torch.equal(pg, p1) and not torch.equal(m1, m0)
+
+
+def test_block_with_e4m3_attention_scores():
+  """The FP8 attention opt-in inside the block (q and k in e4m3 in all four attentions) against the bf16 block: the
+  reference's criterion for its FP8 attention, relative RMS < 0.08 (tests/test_ln_fusions.py:161,181)."""
+  from colabfold_kernels import evoformer, ops
+  g = torch.Generator().manual_seed(5)
+  bf = torch.bfloat16
+  s, r = 16, 128
+  msa, pair = torch.randn(s, r, 256, generator=g).to(bf).cuda(), torch.randn(r, r, 128, generator=g).to(bf).cuda()
+  msa_mask = (torch.rand(s, r, generator=g) < 0.95).float().cuda()
+  pair_mask = (torch.rand(r, r, generator=g) < 0.95).float().cuda()
+  params = evoformer.init_params(seed=6, device="cuda")
+  K = evoformer.cuda_kernels()
+  m0, p0 = evoformer.block(K, msa, pair, msa_mask, pair_mask, params)
+  m1, p1 = evoformer.block(K, msa, pair, msa_mask, pair_mask, params, fp8_attention=True)
+  assert ops.device_status() == 0
+  assert O.rms_err(m1.cpu().float(), m0.cpu().float()) < 0.08
+  assert O.rms_err(p1.cpu().float(), p0.cpu().float()) < 0.08
+  assert not torch.equal(m0, m1) and not torch.equal(p0, p1)  # the e4m3 path really ran
