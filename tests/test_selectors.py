@@ -55,3 +55,32 @@ def test_no_cpu_fallback():
 def test_status_names_cover_the_header():
   assert _lib.STATUS_NAMES[0] == "CFK_OK" and _lib.STATUS_NAMES[-8] == "CFK_ERR_UNSUPPORTED"
   assert "cfk_opm_outer_product" in _lib.PROTOTYPES and "cfk_layer_norm_bwd_static" in _lib.PROTOTYPES
+
+
+def test_fp8_attention_slots_follow_the_reference_rules():
+  """fused_ops.py:75-97 and tests/test_ln_fusions.py:162-172 of the reference: e4m3 slots only when global_config.fp8
+  asks, never below the 8-bit MMA's K of 32, q (with its static scale sm_scale * log2 e) and k where the q.k kernel
+  runs, and the k/v form is then not offered."""
+  on = {**ON, "fp8": True}
+  slots, scales = fused_ops.fp8_attention_slots(on, bf, 32, 264)
+  assert slots == (0, 1) and scales[1] == 1.0 and abs(scales[0] - 32 ** -0.5 * 1.4426950408889634) < 1e-12
+  assert fused_ops.fp8_attention_slots(on, None, 32, 0) is not None  # dtype None: "would any dtype do" (fused_ops.py:80)
+  for d in (8, 16, 48, 64):
+    assert fused_ops.fp8_attention_slots(on, bf, d, 64) is None
+  assert fused_ops.fp8_attention_slots(ON, bf, 32, 64) is None
+  assert fused_ops.fp8_attention_slots(on, torch.float32, 32, 64) is None
+  assert fused_ops.fp8_attention(on, 32) is False and fused_ops.fp8_attention(on, 16) is False
+
+
+def test_reference_restatement_of_the_e4m3_projection_slots():
+  """ref_ln_projection with f8_slots returns (other slots, bias, chosen slots times their scales), packed_attn.py:308-318."""
+  from colabfold_kernels import reference
+  g = torch.Generator().manual_seed(0)
+  x, w, wb = torch.randn(9, 64, generator=g), torch.randn(4, 64, 16, generator=g), torch.randn(64, 2, generator=g)
+  sc, of = torch.ones(64), torch.zeros(64)
+  p, b = reference.ref_ln_projection(x, sc, of, w, wb)
+  ph, b2, p8 = reference.ref_ln_projection(x, sc, of, w, wb, f8_slots=(0, 1), f8_scales=(0.25, 1.0))
+  p = p.reshape(9, 4, 16)
+  assert torch.equal(b, b2)
+  assert torch.allclose(ph.reshape(9, 2, 16), p[:, 2:]) and torch.allclose(p8.reshape(9, 2, 16)[:, 0], 0.25 * p[:, 0])
+  assert torch.allclose(p8.reshape(9, 2, 16)[:, 1], p[:, 1])
