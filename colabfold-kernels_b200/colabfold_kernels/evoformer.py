@@ -61,14 +61,12 @@ def init_params(c_m=256, c_z=128, heads_msa=8, heads_pair=4, d_head=32, c_opm=32
 
 
 def cuda_kernels():
-  """The production namespace: every op is a kernel of libcfk_b200 except the two transitions' GEMMs, which this
-  build leaves to the library GEMM (the fused LN-MLP transition is the next op on the list)."""
+  """The production namespace: every op is a kernel of libcfk_b200 except the second GEMM of the two transitions,
+  which is the library GEMM (LayerNorm, the first GEMM, its bias and the relu are one kernel of the library)."""
   from colabfold_kernels import ops
 
   def transition(x, ln, w1, b1, w2, b2):
-    y = ops.layer_norm(x, ln[0], ln[1])
-    h = torch.relu(torch.addmm(b1, y, w1))
-    return torch.addmm(b2, h, w2) + x
+    return ops.transition(x, ln[0], ln[1], w1, b1, w2, b2, add_input=True)
 
   return types.SimpleNamespace(
       ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,

@@ -242,8 +242,13 @@ def opm_outer(global_config, dtype, rows, num_inner, d, num_output):
 
 
 def transition(global_config, dtype, num_channel, num_intermediate):
-  """The fused LN-MLP transition (fused_ops.py:181-198) has no kernel in this build yet: the caller runs its own path."""
-  return None
+  """-> f(x, ln_scale, ln_offset, w1, b1, w2, b2, keep=None, *, eps, add_input) or None: the LN-MLP transition
+  (fused_ops.py:181-198).  LayerNorm -> first GEMM -> bias -> relu is one kernel of the library; the second GEMM with
+  its bias and the residual is the library GEMM."""
+  if not _half_ok(global_config, dtype) or not _k_ok(num_channel) or num_intermediate % 64 != 0:
+    return None
+  from colabfold_kernels import grads, ops, reference
+  return grads.differentiable_via(ops.transition, reference.ref_transition, nondiff=("eps", "add_input"))
 
 
 def glu_transition(global_config, dtype, num_channel, num_intermediate):

@@ -163,6 +163,26 @@ extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const flo
   return run_chunks(prm, g * cps, w, nullptr, g, n, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int cfk_transition_hidden(const void* x, const float* ln_scale, const float* ln_offset, const void* w1,
+                                     const void* b1, const void* keep, int keep_dtype, void* h_out, int64_t m, int c,
+                                     int hdim, float eps, void* stream) {
+  if (!x || !ln_scale || !ln_offset || !w1 || !b1 || !h_out) return CFK_ERR_NULL;
+  if (m < 0 || hdim <= 0 || hdim % 64 != 0) return CFK_ERR_SHAPE;
+  if (!k_ok(c)) return CFK_ERR_UNSUPPORTED;
+  if (m == 0) return CFK_OK;
+  RowGemmParams prm{};
+  prm.src[0] = row_major(x, c, ln_scale, ln_offset);
+  prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.eps = eps;
+  prm.mode = kModeLinear; prm.dual = 0; prm.relu = 1;
+  prm.n_chunk = (hdim % 128 == 0 && c != 256) ? 128 : 64;  // as in cfk_ln_projection
+  const int cps = hdim / prm.n_chunk;
+  prm.chunks_per_slot = cps; prm.chunks_per_array = cps; prm.bias_slot_stride = 0;
+  prm.bias[0] = b1; prm.bias_len = hdim;
+  prm.out[0] = h_out; prm.ldo = hdim; prm.n_valid = hdim; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
+  return run_chunks(prm, cps, w1, nullptr, 1, hdim, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* ln_offset, const void* wb,
                                 const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
                                 float eps, void* stream) {

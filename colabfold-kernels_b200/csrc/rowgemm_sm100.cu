@@ -606,9 +606,10 @@ rowgemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[0][j] = valid ? y[0][j] * act_sigmoid(y[1][j]) : 0.f;
           } else {
+            const float floor = p.relu ? 0.f : -INFINITY;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              y[0][j] *= mk;
+              y[0][j] = fmaxf(y[0][j], floor) * mk;
               if (DUAL) y[1][j] *= mk;
             }
           }

@@ -40,6 +40,7 @@ struct RowGemmParams {
   int64_t outer, inner, inner_pad;  // tiles = outer * ceil(inner_pad / 128); rows r >= inner are zero padding
   float eps;
   int mode, swish;                  // swish: act = x * sigmoid(x) instead of sigmoid (GDP only)
+  int relu;                         // kModeLinear: max(y, 0) after the bias
   int dual;                         // two accumulators per chunk
   int n_chunk;                      // columns per accumulator and chunk: 16..128, multiple of 16
   int chunks;                       // chunks handled per tile (weights of all of them stay resident)

@@ -205,6 +205,15 @@ CFK_API int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* 
 CFK_API int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, const void* keep,
                                   int keep_dtype, void* out, int64_t m, int k, int c, void* stream);
 
+/* First half of the LN-MLP transition: h[m, hdim] = relu(LN(x) w1 + b1) in bf16; x [m,c], w1 [c,hdim], b1 [hdim];
+ * c in {64,128,256}, hdim a multiple of 64.  keep [m] or NULL: a 128-row block it marks nowhere is written as zeros
+ * (its h contributes nothing to the second GEMM; the caller restores x + b2 there as transition.py:88-92 asks).
+ * Together with a GEMM h w2 + b2 (+ x) it replaces fused_transition, transition.py:100-138 (FFI: volta.py:418-428);
+ * the hidden activation makes one round trip through HBM where the reference keeps it on chip. */
+CFK_API int cfk_transition_hidden(const void* x, const float* ln_scale, const float* ln_offset, const void* w1,
+                                  const void* b1, const void* keep, int keep_dtype, void* h_out, int64_t m, int c,
+                                  int hdim, float eps, void* stream);
+
 /* left, right = mask[m] * (LN(x) lw + lb), mask[m] * (LN(x) rw + rb); x [m,c]; lw, rw [c,k]; k <= 128.
  * Replaces opm_projection, opm.py:36-59. */
 CFK_API int cfk_opm_projection(const void* x, const float* ln_scale, const float* ln_offset, const void* lw,

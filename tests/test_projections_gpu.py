@@ -140,3 +140,38 @@ def test_opm_projection(s, r, c, k):
   assert ops.device_status() == 0
   rl, rrr = O.ref_opm_projection(x, sc, of, lw, lb, rw, rb, mask)
   chk(l, rl); chk(rr, rrr)
+
+
+@pytest.mark.parametrize("m,c,hd", [(59, 128, 512), (4101, 128, 512), (300, 256, 1024), (2000, 64, 256), (260 * 260, 128, 512)])
+@pytest.mark.parametrize("add_input", [False, True])
+def test_transition(m, c, hd, add_input):
+  """relu(LN(x) w1 + b1) w2 + b2 (+ x) against the oracle (transition.py:141-146)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(5)
+  x, w1, b1, w2, b2 = rnd(rng, m, c), rnd(rng, c, hd, s=c ** -.5), rnd(rng, hd, s=.1), rnd(rng, hd, c, s=hd ** -.5), rnd(rng, c, s=.1)
+  sc, of = 1 + rnd(rng, c, s=.1).float(), rnd(rng, c, s=.1).float()
+  out = ops.transition(x.cuda(), sc.cuda(), of.cuda(), w1.cuda(), b1.cuda(), w2.cuda(), b2.cuda(), add_input=add_input)
+  assert ops.device_status() == 0
+  chk(out, O.ref_transition(x, sc, of, w1, b1, w2, b2, add_input=add_input))
+
+
+def test_transition_keep_leaves_padding_blocks_as_the_reference_does():
+  """A 128-row block keep marks nowhere is zeros (x with add_input); marked rows are computed as without keep
+  (transition.py:88-92,108-110)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(6)
+  m, c, hd = 1000, 128, 512
+  x, w1, b1, w2, b2 = rnd(rng, m, c), rnd(rng, c, hd, s=c ** -.5), rnd(rng, hd, s=.1), rnd(rng, hd, c, s=hd ** -.5), rnd(rng, c, s=.1)
+  sc, of = 1 + rnd(rng, c, s=.1).float(), rnd(rng, c, s=.1).float()
+  keep = torch.ones(m)
+  keep[256:640] = 0  # blocks 2, 3 and 4 are padding throughout
+  keep[700] = 0      # a hole in a live block changes nothing
+  args = [t.cuda() for t in (x, sc, of, w1, b1, w2, b2)]
+  for add_input in (False, True):
+    out = ops.transition(*args, keep=keep.cuda(), add_input=add_input)
+    full = ops.transition(*args, add_input=add_input)
+    live = torch.ones(m, dtype=torch.bool)
+    live[256:640] = False
+    assert torch.equal(out[live.cuda()], full[live.cuda()])
+    pad = out[256:640]
+    assert torch.equal(pad, x[256:640].cuda()) if add_input else torch.count_nonzero(pad) == 0

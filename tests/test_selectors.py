@@ -37,7 +37,8 @@ def test_supported_and_declined_shapes():
   assert callable(fused_ops.output_projection(ON, bf, 128, 128)) and fused_ops.output_projection(ON, bf, 128, 12) is None
   assert callable(fused_ops.opm_projection(ON, bf, 256, 32)) and fused_ops.opm_projection(ON, bf, 256, 200) is None
   # ops this build leaves to the caller
-  assert fused_ops.transition(ON, bf, 128, 512) is None and fused_ops.glu_transition(ON, bf, 128, 512) is None
+  assert callable(fused_ops.transition(ON, bf, 128, 512)) and fused_ops.transition(ON, bf, 96, 512) is None
+  assert fused_ops.transition(ON, bf, 128, 100) is None and fused_ops.glu_transition(ON, bf, 128, 512) is None
   # the shallow outer-product forms take the reference's own shape rules (opm.py:88-90,142-144)
   assert callable(fused_ops.opm_update(ON, bf, 64, 128)) and fused_ops.opm_update(ON, bf, 40, 128) is None
   assert callable(fused_ops.opm_outer(ON, bf, 16, 32, 32, 128)) and fused_ops.opm_outer(ON, bf, 8, 32, 32, 128) is None
