@@ -112,7 +112,8 @@ def cpu_arm(steps, warmup, sample_b=32):
 def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False, fp8_attention=False, graph=True):
   """Second metric: one Evoformer block (inference wiring of the fused ops) at N_seq=512, N_res=1024, device-timed,
   max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed).  fp8_trimul: the
-  reference's opt-in e4m3 triangle contraction (half the bytes of the operand the ranks exchange)."""
+  reference's opt-in e4m3 contractions (triangle multiplication: half the bytes of the operand the ranks exchange; and
+  the outer product of the MSA projections).  fp8_attention: e4m3 q and k in the four attentions."""
   import torch
   import torch.distributed as dist
   from colabfold_kernels import evoformer
@@ -125,12 +126,13 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   params = evoformer.init_params(device=dev)
   K = evoformer.cuda_kernels()
   if world > 1:
-    blk = evoformer.ShardedBlock(K, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention)
+    blk = evoformer.ShardedBlock(K, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention, fp8_opm=fp8_trimul)
     msa_l, pair_l = msa[blk.shard(n_seq)].to(dev), pair[blk.shard(n_res)].to(dev)
     run = lambda: blk(msa_l, pair_l, msa_mask, pair_mask)
   else:
     msa_l, pair_l = msa.to(dev), pair.to(dev)
-    run = lambda: evoformer.block(K, msa_l, pair_l, msa_mask, pair_mask, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention)
+    run = lambda: evoformer.block(K, msa_l, pair_l, msa_mask, pair_mask, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention,
+                                  fp8_opm=fp8_trimul)
   for _ in range(2):
     run()
   if world > 1:
@@ -346,7 +348,7 @@ def main():
                    "fwd_ms": fwd, "bwd_ms": bwd, "pct_of_peak": 100.0 * flops(B) / (ms_per_step * 1e-3) / 1e12 / peak_tf,
                    "device_status": status,
                    "evoformer_block": None if block_ms is None else {
-                       "ms": block_ms, "ms_e4m3_trimul": block_f8_ms, "ms_e4m3_trimul_and_attention": block_f8a_ms, "launch": block_launch, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
+                       "ms": block_ms, "ms_e4m3_contractions": block_f8_ms, "ms_e4m3_contractions_and_attention": block_f8a_ms, "launch": block_launch, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
                        "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,

@@ -115,7 +115,7 @@ def transition(K, x, prm):
   return K.transition(x.reshape(-1, shape[-1]), prm["ln"], prm["w1"], prm["b1"], prm["w2"], prm["b2"]).reshape(shape)
 
 
-def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_attention=False):
+def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_attention=False, fp8_opm=False):
   """One Evoformer block on one device.  msa [s, r, c_m], pair [r, r, c_z], msa_mask [s, r], pair_mask [r, r] (0/1).
   fp8_trimul: the triangle-multiplication operands are written and contracted in e4m3 (the reference's opt-in
   fp8_contraction, fused_ops.py:262-275): half the operand bytes, 1.7x the contraction rate, FP8 tolerance."""
@@ -128,7 +128,7 @@ def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_atten
   msa = transition(K, msa, params["msa_transition"])
   o = params["opm"]
   left, right = K.opm_projection(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
-  pair = K.outer_product_mean(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair)
+  pair = K.outer_product_mean(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair, **({"fp8": True} if fp8_opm else {}))
   for name, incoming in (("tri_out", False), ("tri_in", True)):
     t = params[name]
     l, r = K.ln_gated_dual_proj(pair, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], pair_mask.to(pair.dtype),
@@ -148,11 +148,12 @@ class ShardedBlock:
   Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
   replicated.  s and r must be divisible by the world size."""
 
-  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False):
+  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False, fp8_opm=False):
     import torch.distributed as dist
     self.K, self.params, self.dist, self.group = K, params, dist, group
     self.f8 = {"fp8": True} if fp8_trimul else {}  # e4m3 triangle operands: the gathered operand is half the bytes
     self.fa = {"fp8": True} if fp8_attention else {}  # e4m3 q and k in the attentions
+    self.fo = {"fp8": True} if fp8_opm else {}  # e4m3 outer product of the MSA projections
     self.P = dist.get_world_size(group)
     self.rank = dist.get_rank(group)
 
@@ -210,7 +211,7 @@ class ShardedBlock:
     o = prm["opm"]
     mloc = msa_mask[:, rs].contiguous()
     left, right = K.opm_projection(msa_c, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], mloc.to(msa_c.dtype))
-    pair_r = K.outer_product_mean(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r)
+    pair_r = K.outer_product_mean(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r, **self.fo)
     msa_s = self.cols_to_rows(msa_c)
     # 5 triangle multiplication, outgoing edges: local rows of the left operand, all rows of the right
     t = prm["tri_out"]

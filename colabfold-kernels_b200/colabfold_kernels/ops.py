@@ -359,12 +359,16 @@ def opm_finish(x, bias, norm, residual=None, eps=1e-3, out=None):
   return out
 
 
-def _outer_product(left, right):
-  """sum_s left[s,i,c] right[s,j,e] -> [i*j, c*e] bf16, rounded as the reference's opm_outer writes it (opm.py:124-134)."""
+def _outer_product(left, right, fp8=False):
+  """sum_s left[s,i,c] right[s,j,e] -> [i*j, c*e] bf16, rounded as the reference's opm_outer writes it (opm.py:124-134).
+  fp8: the two projections are cast to e4m3 (saturating, unscaled) and the sum runs on the 8-bit tensor-core path."""
   s, ri, c = left.shape
   rj, e = right.shape[1], right.shape[2]
-  a = left.permute(1, 2, 0).reshape(1, ri * c, s).contiguous()       # [(i,c), s]
-  b = right.permute(1, 2, 0).reshape(1, rj * e, s).contiguous()      # [(j,e), s]
+  a = left.permute(1, 2, 0).reshape(1, ri * c, s)       # [(i,c), s]
+  b = right.permute(1, 2, 0).reshape(1, rj * e, s)      # [(j,e), s]
+  if fp8:
+    a, b = (t.clamp(-448.0, 448.0).to(torch.float8_e4m3fn) for t in (a, b))
+  a, b = a.contiguous(), b.contiguous()
   if c == 32 and e == 32 and (s * a.element_size()) % 16 == 0:
     # the kernel stores the product as [i, j, c, e] itself: no transposed copy of the 2*ri*rj*c*e-byte intermediate
     outer = torch.empty((1, ri * rj, c * e), dtype=torch.bfloat16, device=left.device)
@@ -395,13 +399,14 @@ def opm_update(lhs, t, bias, norm, residual=None, eps=1e-3):
   return opm_finish(x, bias, norm, None if residual is None else residual.to(dt), eps)
 
 
-def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3, fp8=False):
   """Deep-MSA outer product mean from the masked projections left [s, ri, c], right [s, rj, c]: two tensor-core GEMMs
   (the outer product over the MSA depth, rounded to bf16 as the reference's opm_outer does, opm.py:124-134; then the
-  output weights w [c*c, f]) and the normalising tail -> [ri, rj, f].  ri < rj when the pair is row-sharded."""
+  output weights w [c*c, f]) and the normalising tail -> [ri, rj, f].  ri < rj when the pair is row-sharded.
+  fp8: the opt-in e4m3 outer product (projections cast to e4m3, fp32 accumulation)."""
   ri, c = left.shape[1], left.shape[2]
   rj, e = right.shape[1], right.shape[2]
-  outer = _outer_product(left, right)
+  outer = _outer_product(left, right, fp8=fp8)
   wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
   x = contract(outer, wt).view(ri, rj, w.shape[1])
   norm = mask_left.float().t() @ mask_right.float()

@@ -132,3 +132,24 @@ def test_contract_gathered_rejects_parts_that_split_a_tile():
   b = torch.zeros(2, 1, 64, 64, dtype=torch.bfloat16, device="cuda")
   with pytest.raises(RuntimeError):
     ops.contract_gathered(a, b)
+
+
+def test_outer_product_mean_e4m3_opt_in():
+  """The FP8 variant casts the two projections to e4m3 (saturating) before the outer product: checked against the
+  oracle on the rounded projections at the bf16 tolerance, and against the unrounded ones at the FP8 tolerance."""
+  from colabfold_kernels import ops
+  s, r = 64, 40
+  rng = np.random.default_rng(9)
+  mk = lambda *sh, sc=.5: torch.from_numpy((rng.standard_normal(sh) * sc).astype(np.float32)).to(torch.bfloat16)
+  mask = torch.from_numpy((rng.random((s, r)) > .1).astype(np.float32))
+  left, right = mk(s, r, 32) * mask[..., None].to(torch.bfloat16), mk(s, r, 32) * mask[..., None].to(torch.bfloat16)
+  left[0, 0, 0] = 1000.0  # beyond e4m3's range: saturates at 448 instead of becoming NaN
+  w, bias, res = mk(32 * 32, 128, sc=1 / 32), mk(128, sc=.1), mk(r, r, 128)
+  got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda(), fp8=True)
+  assert ops.device_status() == 0 and torch.isfinite(got).all()
+  l8, r8 = O.e4m3(left).float(), O.e4m3(right).float()
+  assert float(l8[0, 0, 0]) == 448.0
+  assert O.rel_err(got.cpu().float(), O.ref_opm_deep(l8, r8, mask, w, bias, res)) <= 3e-2
+  left[0, 0, 0] = 0.5
+  got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda(), fp8=True)
+  assert O.rel_err(got.cpu().float(), O.ref_opm_deep(left, right, mask, w, bias, res)) <= 6e-2
