@@ -70,7 +70,7 @@ def _install_numpy_jax():
 
 def main():
   ap = argparse.ArgumentParser()
-  ap.add_argument("--src", default="/root/reference/src")
+  ap.add_argument("--src", required=True, help="the `src` directory of a checkout of the reference (holds colabfold_kernels/)")
   ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
   args = ap.parse_args()
   _install_numpy_jax()
