@@ -167,6 +167,7 @@ def main():
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
   ap.add_argument("--block", type=int, default=1, help="also time one Evoformer block (0 to skip)")
   ap.add_argument("--block-graph", type=int, default=1, help="replay the block as one CUDA graph (0: launch op by op)")
+  ap.add_argument("--e2e-chunks", type=int, default=8, help="pieces the batch is streamed in by the end-to-end step")
   ap.add_argument("--batch", type=int, default=B, help="batch rows per GPU (smaller values are for profiler captures only)")
   args = ap.parse_args()
   globals()["B"] = args.batch
@@ -259,7 +260,7 @@ def main():
   # The step streams the batch through the device in chunks: while chunk c computes, chunk c + 1 is on its way in and the
   # results of chunk c - 1 are on their way out (three streams, two device slots).  Every chunk is one call of the public
   # selector callable and one backward through it; dBias accumulates over the chunks in the bias leaf's gradient.
-  n_chunks = 8 if B % 8 == 0 and B >= 64 else 1
+  n_chunks = args.e2e_chunks if B % args.e2e_chunks == 0 and B >= 8 * args.e2e_chunks else 1
   bc = B // n_chunks
   s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
   names = ("q", "k", "v", "do", "mask_bias")
