@@ -3,8 +3,9 @@
 // One CTA owns one 128-key block of one head for G = 3 batch rows: their K/V tiles stay in shared memory and
 // their dK/dV accumulators stay in TMEM while the CTA sweeps the query blocks.  A "step" is one (query block i,
 // batch row g) pair:
-//   MMA issuer     S = Q K^T and dP = dO V^T into TMEM (one step ahead), then, once the softmax warps have
-//                  published P and dS (bf16, shared memory): dV_g += P^T dO, dK_g += dS^T Q, dQ = dS K
+//   MMA issuers    warp 1: S = Q K^T and dP = dO V^T into TMEM (one step ahead), then, once the softmax warps have
+//                  published P and dS (bf16, shared memory): dV_g += P^T dO, dK_g += dS^T Q; warp 3 (which also
+//                  produces the bias tiles) issues dQ = dS K of the same step beside them
 //   softmax warps  8 warps, thread = (query row, half of the 128 keys): p = 2^(s*log2e - lse) from the forward's
 //                  lse, ds = p * (dp - delta); dBias accumulates over the G batch rows in registers and is
 //                  flushed with vector atomics during the block's last step; the previous step's dQ tile goes
@@ -104,7 +105,7 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     mbar_init(sdp_full, 1);
     mbar_init(sdp_empty, 8);
     mbar_init(pds_full, 8);
-    mbar_init(gemm_done, 1);
+    mbar_init(gemm_done, 2);  // the dV/dK issuer and the dQ issuer each commit once per step
     for (int i = 0; i < 2; ++i) {
       mbar_init(&dq_staged[i], 8);
       mbar_init(&dq_free[i], 1);
@@ -151,14 +152,49 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       }
       __syncwarp();
     } else if (warp == 3) {
-      // ---------------------------------------------------------------- TMA producer: bias tile per query block
-      // (its own warp, so that waiting for the single bias buffer never holds back the Q / dO prefetch)
-      if (lane == 0 && prm.has_bias) {
-        for (int i = 0; i < ni; ++i) {
-          if (!mbar_wait_deadline(bias_empty, (i & 1) ^ 1)) { report_timeout(prm.status, 601); break; }
-          mbar_arrive_expect_tx(bias_full, kTileBig);
-          tma_load_3d(smem + kOffBias, &tm_bias, bias_full, k0, i * kBQ, head);
-          tma_load_3d(smem + kOffBias + kTileBig / 2, &tm_bias, bias_full, k0 + 64, i * kBQ, head);
+      // ---------------------------------------------------------------- bias tile per query block + the dQ GEMM
+      // One thread with two duties it polls for: the bias producer (its own warp, so that waiting for the single bias
+      // buffer never holds back the Q / dO prefetch) and a second MMA issuer.  dQ = dS K of a step goes out from here
+      // while the other issuer sends dV and dK: small MMAs cost an issuing thread ~58 clocks each whatever their tensor
+      // time, two issuing warps ~41.
+      if (lane == 0) {
+        constexpr uint32_t idesc_q = make_idesc(kBQ, D, 1, 1, 0, 1);     // dQ: A = dS (K-major), B = K (MN-major)
+        constexpr uint32_t kTile16 = kTile >> 4;
+        constexpr uint32_t hi64 = desc_hi(8 * kRowBytes, kSwz64);
+        constexpr uint32_t hi128 = desc_hi(1024, kSwz128);
+        const uint32_t k_mn = desc_lo(smem_u32(smem + kOffK), 0);
+        const uint32_t ds_k = desc_lo(smem_u32(smem + kOffDs), 16);
+        const int nbias = prm.has_bias ? ni : 0;
+        int bi = 0, t = 0, g = 0;
+        long long t0 = clock64();
+        while (bi < nbias || t < nsteps) {
+          bool moved = false;
+          if (bi < nbias && mbar_test(bias_empty, (bi & 1) ^ 1)) {
+            mbar_arrive_expect_tx(bias_full, kTileBig);
+            tma_load_3d(smem + kOffBias, &tm_bias, bias_full, k0, bi * kBQ, head);
+            tma_load_3d(smem + kOffBias + kTileBig / 2, &tm_bias, bias_full, k0 + 64, bi * kBQ, head);
+            ++bi;
+            moved = true;
+          }
+          if (t < nsteps && mbar_test(pds_full, t & 1)) {
+            tc_fence_after();
+            const uint32_t bk = k_mn + g * kTile16;
+            // dQ = dS K: A K-major (64 keys per 128-byte row, second half 16 KB on), a K step is 16 keys
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_f16_ss2(tmem + kColDq, ds_k + (kk / 4) * (kTileBig / 32) + (kk % 4) * 2, hi128, bk + kk * 64, hi64, idesc_q,
+                          kk > 0);
+            mma_commit(gemm_done);
+            ++t;
+            if (++g == gcount) g = 0;
+            moved = true;
+          }
+          if (moved) {
+            t0 = clock64();
+          } else if (clock64() - t0 > (1ll << 30)) {
+            report_timeout(prm.status, 601);
+            break;
+          }
         }
       }
       __syncwarp();
@@ -228,11 +264,7 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #pragma unroll
           for (int kk = 0; kk < kBQ / 16; ++kk)
             mma_f16_ss2(d_k, ds_mn + kk * 128, hi128, bq + kk * 64, hi64, idesc_t, kk > 0 ? 1u : acc0);
-          // dQ = dS K: A K-major (64 keys per 128-byte row, second half 16 KB on), a K step is 16 keys
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16_ss2(tmem + kColDq, ds_k + (kk / 4) * (kTileBig / 32) + (kk % 4) * 2, hi128, bk + kk * 64, hi64, idesc_q,
-                        kk > 0);
+          // (dQ = dS K of the step is issued by the second issuer, warp 3)
           mma_commit(&qdo_empty[o_st]);
           mma_commit(gemm_done);
           pf_par ^= 1;
