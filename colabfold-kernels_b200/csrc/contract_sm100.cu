@@ -112,7 +112,10 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = prm.is_f8 ? make_idesc(kTM, kTN, 0, 0, 0, 0) : make_idesc(kTM, kTN, 1, 1, 0, 0);
+      // a product no wider than 128 columns (the outer product mean's output weights) runs N = 128 instructions: the
+      // rows of the B box past J are fill values and their half of the accumulator would only hold zeros
+      const uint32_t nn = prm.J <= 128 ? 128u : uint32_t(kTN);
+      const uint32_t idesc = prm.is_f8 ? make_idesc(kTM, nn, 0, 0, 0, 0) : make_idesc(kTM, nn, 1, 1, 0, 0);
       const uint32_t a_base = smem_u32(smem + kOffA), b_base = smem_u32(smem + kOffB);
       int it = 0, n = 0;
       bool ok = true;
@@ -155,7 +158,7 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < (prm.J <= 128 ? 1 : 2); ++half) {
         if (issuer) tma_wait_group_read<0>();  // the previous store has finished reading the staging tile
         named_bar_sync(1, 128);
 #pragma unroll
