@@ -165,6 +165,12 @@ class _PackedAttention(torch.autograd.Function):
     q, k, v = (pp[:, :, i].contiguous() for i in range(3))  # seq-major [b, s, h, d]
     o_att, lse = ops.attention_fwd(q, k, v, bias, kmask, sm_scale, seq_major=True, want_lse=True)
     do = do.contiguous()
+    if trim:
+      # the trimmed forward writes zeros for batch rows without a live key and for queries past the last live key of
+      # any row (packed_attn.py:132-137): those outputs carry no gradient
+      lim = ops.trim_limits(kmask)
+      rows = (lim[:-1] > 0)[:, None] & (torch.arange(do.shape[1], device=do.device) < lim[-1])[None, :]
+      do = do * rows[:, :, None, None].to(do.dtype)
     dg = None
     if gated:
       sig = torch.sigmoid(pp[:, :, 3].float() + gate_bias.float())

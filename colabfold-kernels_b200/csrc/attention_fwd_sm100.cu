@@ -4,18 +4,28 @@
 // per-head bias (the bias is read once per key block and reused for G score tiles).  A "step" is one
 // (key block j, batch row g) pair; steps alternate between two softmax groups so that one group's
 // exponentials overlap the other's MMAs.  Warp roles (warpgroup 0 hands its registers to the others):
-//   warp 0      TMA producer: Q tiles (once), bias tile per key block, K tile per step
-//   warp 1      MMA issuer:   S = Q K^T (SS, two steps ahead), O += P V (TS: P is read from TMEM)
-//   warp 2      key-mask producer: per step 128 additive floats (0 / floor / -inf) in shared memory
-//   warp 3      TMA producer: V tile per step
+//   warp 0      TMA producer: Q tiles (once), bias tile per key block, K and V tiles per step
+//   warp 1      MMA issuer:   S = Q K^T + the mask step (SS, two steps ahead)
+//   warp 2      key-mask producer: per step the additive key mask (0 / floor / lower floor) in shared memory
+//   warp 3      MMA issuer:   O += P V (TS: P is read from TMEM)
 //   warps 4-7   softmax group 0 (batch rows 0, 2, ...), one thread per query row = one TMEM lane
 //   warps 8-11  softmax group 1 (batch rows 1, 3, ...)
 // TMEM columns: S0 [0,128) S1 [128,256) | P0 [256,320) P1 [320,384) (bf16 pairs) | O_g [384 + g*D, +D).
-// Softmax is online in the natural-log domain with a lazily updated reference maximum; masked keys are an
-// additive per-key floor, keys past Sk an additive -inf.  Every barrier wait is deadline-bounded and reports
-// into the status word instead of hanging.  The MMA-issuing thread is scalar code on one lane: it only adds
-// constants to descriptors built once, because every extra instruction there delays the tensor pipe.
+// Softmax is online with a lazily updated reference maximum; masked keys are an additive per-key floor, keys past
+// Sk a lower one.  Every barrier wait is deadline-bounded and reports into the status word instead of hanging.
+// The MMA-issuing thread is scalar code on one lane: it only adds constants to descriptors built once, because
+// every extra instruction there delays the tensor pipe.
+//
+// At head dim 32 the softmax warps' instruction stream, not the tensor pipe, sets the pace (64 tensor flops per score
+// against one ex2 and a handful of fp32 instructions), so the key mask is added by the tensor pipe: after Q K^T the
+// scores accumulator receives one K = 16 step [1 0 ..] x [mask 0 ..]^T (a column of ones beside Q, the additive mask in
+// accumulator units beside K).  (The bias was tried the same way - eight K = 16 steps (I / scale) x bias tile - and
+// dropped: an M = 128 MMA reads 8 KB of shared memory whatever it computes, and eight of them per step cost more of
+// the shared-memory path than the bias add costs the softmax warps.)
 // Math: src/colabfold_kernels/tri_flash.py:132-167,215-239; gate: packed_attn.py:157-158.
+#include <cmath>
+#include <cstring>
+
 #include "attention_sm100.cuh"
 
 namespace cfk {
@@ -39,8 +49,11 @@ struct FwdCfg {
   static constexpr int kOffV = kOffK + kStages * kTileQK;
   static constexpr int kOffBias = kOffV + kStages * kTileV;
   static_assert(kOffV % 1024 == 0 && kOffBias % 1024 == 0, "swizzled tiles start on their atom");
-  static constexpr int kOffMask = kOffBias + 2 * kTileBias;         // float [kMaskSlots][128] additive key mask
-  static constexpr int kOffFlag = kOffMask + kMaskSlots * 128 * 4;  // int [kMaskSlots]: any key masked / past Sk
+  static constexpr int kTileAug = kBQ * 32;  // [128 rows][16 bf16]: the extra K = 16 step (32-byte rows, 32-byte swizzle)
+  static constexpr int kOffQaug = kOffBias + 2 * kTileBias;        // column of ones
+  static constexpr int kOffKaug = kOffQaug + kTileAug;             // [kMaskSlots] additive key masks
+  static constexpr int kOffFlag = kOffKaug + kMaskSlots * kTileAug;
+  static_assert(kOffQaug % 1024 == 0 && kOffKaug % 1024 == 0, "swizzled tiles start on their atom");
   static constexpr int kOffState = kOffFlag + 16;                   // float [2][G][128]: reference max, row sum
   static constexpr int kOffBar = kOffState + 2 * G * 128 * 4;
   static constexpr int kNumBars = G + 4 * kStages + 4 + 4 + 4 + 2 * kMaskSlots;
@@ -60,6 +73,15 @@ struct FwdParams {
   int* status;
   int has_bias;
 };
+
+// bf16 bits of the additive key mask in accumulator units (before the scale): a masked key -2^100, a key past Sk -2^126.
+constexpr uint32_t kMaskedBf16 = 0xF180u, kPastEndBf16 = 0xFE80u;
+// A row maximum (scale * accumulator + bias) below this saw masked keys only.  Such a row's logits are all the same
+// number F = fl(-scale * 2^100): the exponent argument is then formed as (t - m) * 2^-90 - exact, 0 on the row's real
+// keys and hugely negative past Sk - instead of fma(t, log2 e, -m log2 e), whose rounding residue would be of the
+// order of 2^73 there.  The row then averages its real keys, as the reference defines.
+constexpr float kDeadNat = -1e25f;
+constexpr float kDeadLk = 8.077935669463161e-28f;  // 2^-90
 
 template <int D, int F8>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -124,13 +146,23 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     }
     for (int i = 0; i < C::kMaskSlots; ++i) {
       mbar_init(&mask_full[i], 1);
-      mbar_init(&mask_empty[i], 4);
+      mbar_init(&mask_empty[i], 1);  // released by the scores issuer's commit
     }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_bias);
+  }
+  {
+    // constant operands: a column of ones, and zeros in the mask ring beyond its first column
+    for (int idx = threadIdx.x; idx < 128 * 2; idx += kThreads) {
+      const int r = idx >> 1, chunk = idx & 1;
+      *reinterpret_cast<uint4*>(smem + C::kOffQaug + swz_off(r, chunk, 32)) = make_uint4(chunk == 0 ? 0x3F80u : 0u, 0, 0, 0);
+    }
+    for (int idx = threadIdx.x; idx < C::kMaskSlots * 128 * 2; idx += kThreads)
+      *reinterpret_cast<uint4*>(smem + C::kOffKaug + idx * 16) = make_uint4(0, 0, 0, 0);
+    fence_proxy_async();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -142,7 +174,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");  // (168 - 64) * 128 registers released ...
     if (warp == 0) {
       // ---------------------------------------------------------------- TMA producer: Q, bias, K
       if (lane == 0) {
@@ -168,26 +200,30 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             if (!ok) { report_timeout(prm.status, 102); break; }
             mbar_arrive_expect_tx(&k_full[st], C::kTileQK);
             tma_load_4d(smem + C::kOffK + st * C::kTileQK, &tm_k, &k_full[st], 0, j * kBK, head, b0 + g);
+            // the V slot of a step frees long before its K slot is wanted again (the scores run two steps ahead of
+            // P V), so waiting for it here never holds a K load back
+            ok = mbar_wait_deadline(&v_empty[st], ((step / ST) & 1) ^ 1);
+            if (!ok) { report_timeout(prm.status, 103); break; }
+            mbar_arrive_expect_tx(&v_full[st], C::kTileV);
+            tma_load_4d(smem + C::kOffV + st * C::kTileV, &tm_v, &v_full[st], 0, j * kBK, head, b0 + g);
           }
         }
       }
       __syncwarp();
-    } else if (warp == 3) {
-      // ---------------------------------------------------------------- TMA producer: V
-      if (lane == 0) {
-        for (int step = 0; step < nsteps; ++step) {
-          const int st = step % ST, g = step % gcount, j = step / gcount;
-          if (!mbar_wait_deadline(&v_empty[st], ((step / ST) & 1) ^ 1)) { report_timeout(prm.status, 103); break; }
-          mbar_arrive_expect_tx(&v_full[st], C::kTileV);
-          tma_load_4d(smem + C::kOffV + st * C::kTileV, &tm_v, &v_full[st], 0, j * kBK, head, b0 + g);
-        }
-      }
-      __syncwarp();
-    } else if (warp == 1) {
-      // ---------------------------------------------------------------- MMA issuer
+    } else if (warp == 1 || warp == 3) {
+      // ---------------------------------------------------------------- MMA issuers: warp 1 the scores, warp 3 P V
+      // Two threads, because what bounds a step is the issuing thread's own instruction chain (waits, descriptor
+      // arithmetic, commits: ~650 clocks per scores step and as much per P V step when one thread did both in turn),
+      // not the tensor pipe, which is a tenth busy.  The two chains touch different TMEM columns and barriers.
       if (lane == 0) {
         constexpr uint32_t idesc_s = F8 ? make_idesc(kBQ, kBK, 0, 0, 0, 0) : make_idesc(kBQ, kBK, 1, 1, 0, 0);
         constexpr uint32_t idesc_pv = make_idesc(kBQ, D, 1, 1, 0, 1);
+        // the mask step: both operands K-major, 32-byte rows
+        constexpr uint32_t idesc_aug = make_idesc(kBQ, kBK, 1, 1, 0, 0);
+        const uint64_t qaug_desc = desc_k_major(smem_u32(smem + C::kOffQaug), 32);
+        const uint64_t kaug_desc0 = desc_k_major(smem_u32(smem + C::kOffKaug), 32);
+        int m_slot = 0;
+        uint32_t m_par = 0;
         constexpr uint32_t kTile16 = C::kTileQK >> 4, kTile16V = C::kTileV >> 4;
         const uint64_t q_desc0 = desc_k_major(smem_u32(smem + C::kOffQ), C::kRowBytesQK);
         const uint64_t k_desc0 = desc_k_major(smem_u32(smem + C::kOffK), C::kRowBytesQK);
@@ -203,6 +239,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (s_first && !mbar_wait_deadline(&q_full[s_g], 0)) { report_timeout(prm.status, 201); return false; }
           if (!mbar_wait_deadline(&k_full[s_st], k_par)) { report_timeout(prm.status, 202); return false; }
           if (!mbar_wait_deadline(&s_empty[buf], buf ? se_par1 : se_par0)) { report_timeout(prm.status, 203); return false; }
+          if (!mbar_wait_deadline(&mask_full[m_slot], m_par)) { report_timeout(prm.status, 206); return false; }
           tc_fence_after();
           const uint64_t a = q_desc0 + uint64_t(s_g * kTile16), b = k_desc0 + uint64_t(s_st * kTile16);
           const uint32_t d = tmem + C::kColS + buf * kBK;
@@ -211,6 +248,9 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             if (F8) mma_f8_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
             else mma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0);
           }
+          mma_f16_ss(d, qaug_desc, kaug_desc0 + uint64_t(m_slot * (C::kTileAug >> 4)), idesc_aug, 1);
+          mma_commit(&mask_empty[m_slot]);
+          if (++m_slot == C::kMaskSlots) { m_slot = 0; m_par ^= 1; }
           mma_commit(&k_empty[s_st]);
           mma_commit(&s_full[buf]);
           if (buf) se_par1 ^= 1; else se_par0 ^= 1;
@@ -236,53 +276,56 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (++p_st == ST) { p_st = 0; v_par ^= 1; }
           return true;
         };
-        ok = issue_s();
-        if (ok && nsteps > 1) ok = issue_s();
-        // S of step t + 2 goes out as soon as its buffer has been read (early in step t), before this thread blocks on
-        // the P of step t: the group then finds its next scores ready when it finishes a step
-        for (int t = 0; t < nsteps && ok; ++t) {
-          if (t + 2 < nsteps) ok = issue_s();
-          if (ok) ok = issue_pv();
+        // the scores of a step go out as soon as their buffer has been read (one per softmax group: two steps ahead)
+        if (warp == 1) {
+          for (int t = 0; t < nsteps && ok; ++t) ok = issue_s();
+        } else {
+          for (int t = 0; t < nsteps && ok; ++t) ok = issue_pv();
         }
       }
       __syncwarp();
     } else {
       // ---------------------------------------------------------------- key-mask producer
-      // Per step: 128 additive floats (0 live, floor masked, -inf past Sk) and an "any" flag, a few steps ahead
-      // of the softmax groups so the global-memory latency is off their critical path.
-      float* mask_ring = reinterpret_cast<float*>(smem + C::kOffMask);
-      int* flag_ring = reinterpret_cast<int*>(smem + C::kOffFlag);
+      // Per step the first column of a [128 keys][16] bf16 operand (the rest stays zero): 0 live, -2^100 masked,
+      // -2^126 past Sk.  The mask bytes of the next step are fetched before this step's slot is waited for, so the
+      // global-memory latency is off the path.
       bool ok = true;
+      auto fetch = [&](int t) -> uint32_t {
+        const int g = t % gcount, j = t / gcount, key = j * kBK + lane * 4;
+        // Sk is a multiple of 8, so a group of four keys is in or out as a whole
+        if (t >= nsteps || key >= p.sk) return 0xffffffffu;  // placeholder, not used for keys past Sk
+        return *reinterpret_cast<const uint32_t*>(p.kmask + int64_t(b0 + g) * p.sk + key);
+      };
+      uint32_t w_next = fetch(0);
       for (int t = 0; t < nsteps && ok; ++t) {
-        const int g = t % gcount, j = t / gcount, slot = t % C::kMaskSlots;
+        const int j = t / gcount, slot = t % C::kMaskSlots;
+        const uint32_t w = w_next;
+        w_next = fetch(t + 1);
         if (lane == 0) ok = mbar_wait_deadline(&mask_empty[slot], ((t / C::kMaskSlots) & 1) ^ 1);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) { if (lane == 0) report_timeout(prm.status, 501); break; }
-        const int key = j * kBK + lane * 4;
-        float4 add = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        if (key < p.sk) {  // Sk is a multiple of 8, so a group of four keys is in or out as a whole
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(p.kmask + int64_t(b0 + g) * p.sk + key);
-          add.x = (w & 0x000000ffu) ? 0.f : kFloorNat;
-          add.y = (w & 0x0000ff00u) ? 0.f : kFloorNat;
-          add.z = (w & 0x00ff0000u) ? 0.f : kFloorNat;
-          add.w = (w & 0xff000000u) ? 0.f : kFloorNat;
-        }
-        *reinterpret_cast<float4*>(mask_ring + slot * 128 + lane * 4) = add;
-        const unsigned any = __ballot_sync(0xffffffffu, add.x != 0.f || add.y != 0.f || add.z != 0.f || add.w != 0.f);
-        if (lane == 0) flag_ring[slot] = any != 0;
+        const bool in = j * kBK + lane * 4 < p.sk;
+        const uint32_t m0 = !in ? kPastEndBf16 : (w & 0x000000ffu) ? 0u : kMaskedBf16;
+        const uint32_t m1 = !in ? kPastEndBf16 : (w & 0x0000ff00u) ? 0u : kMaskedBf16;
+        const uint32_t m2 = !in ? kPastEndBf16 : (w & 0x00ff0000u) ? 0u : kMaskedBf16;
+        const uint32_t m3 = !in ? kPastEndBf16 : (w & 0xff000000u) ? 0u : kMaskedBf16;
+        uint8_t* tile = smem + C::kOffKaug + slot * C::kTileAug;
+        *reinterpret_cast<uint4*>(tile + swz_off(lane * 4 + 0, 0, 32)) = make_uint4(m0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(tile + swz_off(lane * 4 + 1, 0, 32)) = make_uint4(m1, 0, 0, 0);
+        *reinterpret_cast<uint4*>(tile + swz_off(lane * 4 + 2, 0, 32)) = make_uint4(m2, 0, 0, 0);
+        *reinterpret_cast<uint4*>(tile + swz_off(lane * 4 + 3, 0, 32)) = make_uint4(m3, 0, 0, 0);
+        fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&mask_full[slot]);
       }
     }
   } else {
     // ------------------------------------------------------------------ softmax groups
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");  // ... cover the (216 - 168) * 256 taken here
     const int grp = (warp - 4) >> 2;           // 0 or 1
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may touch
     const int row = quad * 32 + lane;          // query row inside the tile = TMEM lane
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    const float* mask_ring = reinterpret_cast<const float*>(smem + C::kOffMask);
-    const int* flag_ring = reinterpret_cast<const int*>(smem + C::kOffFlag);
     // running (reference maximum, row sum) of each batch row this thread serves: [g][row], private to the thread
     float* st_m = reinterpret_cast<float*>(smem + C::kOffState) + row;
     float* st_l = st_m + G * 128;
@@ -302,7 +345,6 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (prm.has_bias) CFK_SOFTMAX_WAIT(&bias_full[j & 1], (j >> 1) & 1, 301)
 #pragma unroll 1
       for (int g = grp; g < gcount; g += 2) {
-        const int t = j * gcount + g, slot = t % C::kMaskSlots;
 
         CFK_SOFTMAX_WAIT(&s_full[grp], uses & 1, 302)
         tc_fence_after();
@@ -315,7 +357,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[grp]);
 
-        // logits t = scale * s + bias (+ mask), row maximum; packed fp32 pairs: two keys per FMA-pipe instruction
+        // logits t = scale * s + bias (the mask is in s already); packed fp32 pairs: two keys per FMA-pipe instruction
         const uint64_t scale2 = f2_pack(scale, scale);
         if (prm.has_bias) {
 #pragma unroll
@@ -331,24 +373,14 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #pragma unroll
           for (int i = 0; i < kBK; i += 2) f2_unpack(f2_mul(f2_pack(s[i], s[i + 1]), scale2), s[i], s[i + 1]);
         }
-        CFK_SOFTMAX_WAIT(&mask_full[slot], (t / C::kMaskSlots) & 1, 305)
-        if (flag_ring[slot] != 0) {
-#pragma unroll
-          for (int c = 0; c < kBK / 4; ++c) {
-            const float4 a = *reinterpret_cast<const float4*>(mask_ring + slot * 128 + c * 4);
-            f2_unpack(f2_add(f2_pack(s[c * 4 + 0], s[c * 4 + 1]), f2_pack(a.x, a.y)), s[c * 4 + 0], s[c * 4 + 1]);
-            f2_unpack(f2_add(f2_pack(s[c * 4 + 2], s[c * 4 + 3]), f2_pack(a.z, a.w)), s[c * 4 + 2], s[c * 4 + 3]);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&mask_empty[slot]);
         float mx;
         {
-          // four independent chains: two warps per scheduler cannot hide a 128-long dependent chain
+          // four independent chains of three-input maxima: one instruction per two scores
           float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < kBK; i += 4) {
-            m0 = fmaxf(m0, s[i]); m1 = fmaxf(m1, s[i + 1]); m2 = fmaxf(m2, s[i + 2]); m3 = fmaxf(m3, s[i + 3]);
+          for (int i = 0; i < kBK; i += 8) {
+            m0 = fmax3(m0, s[i], s[i + 1]); m1 = fmax3(m1, s[i + 2], s[i + 3]);
+            m2 = fmax3(m2, s[i + 4], s[i + 5]); m3 = fmax3(m3, s[i + 6], s[i + 7]);
           }
           mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
         }
@@ -365,27 +397,34 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             need = true;
           }
         }
-        const float neg_m = -m_ref * kLog2eF;
-        // stage by stage over the whole row (128 independent elements per stage), so that the exponentials overlap
+        // exponent arguments fma(t, lk, -m lk); a row that has seen masked keys only takes lk = 2^-90 (see kDeadNat)
+        const float lk = m_ref < kDeadNat ? kDeadLk : kLog2eF;
+        const float neg_m = -m_ref * lk;
         uint32_t pk[kBK / 2];
         {
-          const uint64_t l2e2 = f2_pack(kLog2eF, kLog2eF), negm2 = f2_pack(neg_m, neg_m);
+          // Software-pipelined by hand and pinned (volatile): each slot issues the two exponentials of one pair of keys,
+          // the multiply-add that prepares the pair two slots on, and the sum and bf16 pack of the pair three slots
+          // back.  The XU pipe (16 ex2 per clock and SM, 8 clocks per warp instruction) is the busiest unit of this
+          // kernel; a warp issues in order, so exponentials written as one run would leave the other pipes idle.
+          const uint64_t l2e2 = f2_pack(lk, lk), negm2 = f2_pack(neg_m, neg_m);
+          uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
+          constexpr int NP = kBK / 2, kAhead = 2, kBehind = 3;
+          uint64_t v[NP];
 #pragma unroll
-          for (int i = 0; i < kBK; i += 2) f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), l2e2, negm2), s[i], s[i + 1]);
+          for (int i = 0; i < kAhead; ++i) v[i] = f2_fma_pinned(f2_pack(s[2 * i], s[2 * i + 1]), l2e2, negm2);
 #pragma unroll
-          for (int i = 0; i < kBK; ++i) s[i] = ex2_approx(s[i]);
-          uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a, sum_c = sum_a, sum_d = sum_a;
-#pragma unroll
-          for (int i = 0; i < kBK; i += 8) {
-            sum_a = f2_add(sum_a, f2_pack(s[i], s[i + 1]));
-            sum_b = f2_add(sum_b, f2_pack(s[i + 2], s[i + 3]));
-            sum_c = f2_add(sum_c, f2_pack(s[i + 4], s[i + 5]));
-            sum_d = f2_add(sum_d, f2_pack(s[i + 6], s[i + 7]));
+          for (int i = 0; i < NP + kBehind; ++i) {
+            if (i < NP) v[i] = f2_ex2_pinned(v[i]);
+            if (i + kAhead < NP)
+              v[i + kAhead] = f2_fma_pinned(f2_pack(s[2 * (i + kAhead)], s[2 * (i + kAhead) + 1]), l2e2, negm2);
+            if (i >= kBehind) {
+              const int k = i - kBehind;
+              if (k & 1) sum_b = f2_add_pinned(sum_b, v[k]); else sum_a = f2_add_pinned(sum_a, v[k]);
+              pk[k] = f2_pack_bf16_pinned(v[k]);
+            }
           }
-#pragma unroll
-          for (int i = 0; i < kBK / 2; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
           float t0, t1;
-          f2_unpack(f2_add(f2_add(sum_a, sum_b), f2_add(sum_c, sum_d)), t0, t1);
+          f2_unpack(f2_add(sum_a, sum_b), t0, t1);
           st_m[g * 128] = m_ref;
           st_l[g * 128] = l_run * corr + (t0 + t1);
         }
@@ -467,7 +506,7 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             *reinterpret_cast<uint4*>(out + c * 8) = w;
           }
           if (p.lse != nullptr)
-            p.lse[(int64_t(b) * p.h + head) * p.sq + q] = m_ref < -1e30f ? kNegRef : fmaf(m_ref, kLog2eF, __log2f(l_run));
+            p.lse[(int64_t(b) * p.h + head) * p.sq + q] = m_ref < kDeadNat ? kNegRef : fmaf(m_ref, kLog2eF, __log2f(l_run));
         }
       }
     }
@@ -525,10 +564,8 @@ bool attention_sm100_supported(const AttnProblem& p, int dtype) {
 }
 
 int attention_fwd_sm100(const AttnProblem& p, cudaStream_t st) {
-  switch (p.d) {
-    case 32: return p.qk_e4m3 ? launch<32, 1>(p, st) : launch<32, 0>(p, st);
-    default: return CFK_ERR_UNSUPPORTED;
-  }
+  if (p.d != 32 || !(p.scale > 0.f)) return CFK_ERR_UNSUPPORTED;
+  return p.qk_e4m3 ? launch<32, 1>(p, st) : launch<32, 0>(p, st);
 }
 
 }  // namespace cfk

@@ -1,5 +1,6 @@
 // Tensor-map construction and the device status word shared by every kernel of the library.
 #include "cfk_common.cuh"
+#include "cfk_ptx.cuh"
 
 #include <cudaTypedefs.h>
 #include <atomic>
@@ -52,24 +53,59 @@ namespace {
 std::atomic<long long> g_launches{0};
 constexpr int kMaxDevices = 64;
 int* g_status[kMaxDevices] = {};
+volatile int* g_mirror[kMaxDevices] = {};  // pinned host copies of the status words
 std::mutex g_status_mutex;
 }  // namespace
 
-void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int note_launch() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CFK_OK;
+  volatile int* m = g_mirror[dev];
+  return (m != nullptr && *m != 0) ? CFK_ERR_DEVICE_WAIT : CFK_OK;
+}
 
-// One int32 per device, allocated on first use on that device and kept for the life of the process.
+// 16 bytes per device (layout in cfk_common.cuh), allocated with their pinned host mirror on first use on that device
+// and kept for the life of the process.
 int* device_status_word() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(g_status_mutex);
   if (g_status[dev] == nullptr) {
     int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-    cudaMemset(p, 0, sizeof(int));
+    int* host = nullptr;
+    int* host_dev = nullptr;
+    if (cudaMalloc(&p, 16) != cudaSuccess) return nullptr;
+    if (cudaHostAlloc(&host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
+      *host = 0;
+      if (cudaHostGetDevicePointer(&host_dev, host, 0) != cudaSuccess) host_dev = nullptr;
+    }
+    unsigned long long words[2] = {0ull, reinterpret_cast<unsigned long long>(host_dev)};
+    if (cudaMemcpy(p, words, 16, cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    g_mirror[dev] = host_dev != nullptr ? host : nullptr;
     g_status[dev] = p;
   }
   return g_status[dev];
 }
+
+namespace {
+// One CTA waits, with a limit of the given number of clocks, on an mbarrier that nothing arrives on, reports the
+// timeout and returns.
+__global__ void wait_selftest_kernel(int* status, long long limit_clocks, int code) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const long long t0 = clock64();
+    bool flipped = false;
+    while (!flipped && clock64() - t0 < limit_clocks) flipped = mbar_try_wait(&bar, 0);
+    if (!flipped) report_timeout(status, code);
+  }
+}
+}  // namespace
 
 }  // namespace cfk
 
@@ -78,12 +114,25 @@ extern "C" int cfk_last_device_status(int reset) {
   if (p == nullptr) return CFK_ERR_LAUNCH;
   int v = 0;
   if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return CFK_ERR_LAUNCH;
-  if (reset && v != 0) cudaMemset(p, 0, sizeof(int));
+  if (reset && v != 0) {
+    cudaMemset(p, 0, sizeof(int));
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < cfk::kMaxDevices && cfk::g_mirror[dev] != nullptr)
+      *cfk::g_mirror[dev] = 0;
+  }
   return v;
+}
+
+extern "C" int cfk_debug_wait_timeout(int64_t limit_clocks, int code, void* stream) {
+  if (limit_clocks <= 0 || limit_clocks > (1ll << 24) || code <= 0) return CFK_ERR_SHAPE;
+  int* status = cfk::device_status_word();
+  if (status == nullptr) return CFK_ERR_LAUNCH;
+  cfk::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_clocks, code);
+  return cfk::check_launch();
 }
 
 extern "C" long long cfk_launch_count(int reset) {
   return reset ? cfk::g_launches.exchange(0) : cfk::g_launches.load();
 }
 
-extern "C" const char* cfk_version() { return "cfk_b200 0.1 (sm_100a)"; }
+extern "C" const char* cfk_version() { return "cfk_b200 0.2 (sm_100a)"; }

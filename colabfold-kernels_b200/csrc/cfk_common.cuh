@@ -11,19 +11,30 @@
 
 namespace cfk {
 
-// Device-side status word layout (one int32 per library, see cfk_status.cu): 0 = ok, else the id of the
-// first wait that ran out of polls.
+// Device-side status word (16 bytes of device memory per device): word 0 is 0 or the id of the first bounded wait that
+// ran out; bytes 8..15 hold the device-visible address of a pinned host int that receives a copy of that id, so that
+// the host entry points can see a pending timeout without synchronising.
 __device__ __forceinline__ void report_timeout(int* status, int code) {
-  if (status != nullptr) atomicCAS(status, 0, code);
+  if (status == nullptr) return;
+  if (atomicCAS(status, 0, code) == 0) {
+    int* mirror = *reinterpret_cast<int* const*>(status + 2);
+    if (mirror != nullptr) {
+      *reinterpret_cast<volatile int*>(mirror) = code;
+      __threadfence_system();
+    }
+  }
 }
 
-// Every kernel launch of the library goes through check_launch(): it counts the launch (cfk_launch_count)
-// and turns a refused launch into a status.
-void note_launch();
+// Every kernel launch of the library goes through check_launch(): it counts the launch (cfk_launch_count), turns a
+// refused launch into CFK_ERR_LAUNCH, and answers CFK_ERR_DEVICE_WAIT while a timeout reported by an earlier kernel
+// on this device has not been read and cleared with cfk_last_device_status(1): kernels launched in that state return
+// at once and write nothing, so their outputs must not be taken for results.
+int note_launch();
 inline int check_launch() {
-  note_launch();
+  const int pending = note_launch();
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? CFK_OK : CFK_ERR_LAUNCH;
+  if (e != cudaSuccess) return CFK_ERR_LAUNCH;
+  return pending;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

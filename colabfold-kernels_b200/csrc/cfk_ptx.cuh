@@ -295,6 +295,46 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Volatile forms: statements that keep their order relative to one another, for hand-scheduled sequences that
+// alternate XU-pipe and FMA-pipe instructions (a warp issues in order: a run of exponentials leaves the FMA pipe idle
+// and the other way round).
+__device__ __forceinline__ uint64_t f2_fma_pinned(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm volatile("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add_pinned(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm volatile("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// 2^lo, 2^hi of a packed pair, as two XU instructions
+__device__ __forceinline__ uint64_t f2_ex2_pinned(uint64_t x) {
+  uint64_t y;
+  asm volatile(
+      "{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tex2.approx.ftz.f32 a, a;\n\tex2.approx.ftz.f32 b, b;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(y)
+      : "l"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t f2_pack_bf16_pinned(uint64_t v) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.bf16x2.f32 %0, b, a;\n\t}" : "=r"(r) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// The same instruction as a volatile statement: it keeps its place between the volatile barrier operations around a
+// phase of exponentials.
+__device__ __forceinline__ float ex2_approx_pinned(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -268,12 +268,9 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
   }
   ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0, part_rows};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
-      return CFK_ERR_LAUNCH;
-    attr_set = true;
-  }
+  // a function attribute belongs to the current device: set on every launch, as the other launchers do
+  if (cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    return CFK_ERR_LAUNCH;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

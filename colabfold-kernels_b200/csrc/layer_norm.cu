@@ -222,13 +222,11 @@ __global__ void ln_bwd_fold_kernel(const float* __restrict__ partial, float* __r
   else doffset[i - c] = s;
 }
 
+// SM count of the current device (asked for on every call: a process may drive several devices)
 int sm_count() {
-  static int n = [] {
-    int dev = 0, v = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    return v;
-  }();
-  return n;
+  int dev = 0, v = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v;
 }
 
 constexpr int kBwdBlocksPerSm = 2;

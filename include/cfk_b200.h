@@ -1,11 +1,21 @@
 /* C ABI of libcfk_b200.so: the B200 (sm_100a) kernels behind colabfold-kernels' Evoformer hot path.
  *
  * Conventions (modelled on the reference's own native FFI, src/colabfold_kernels/volta.py:100-461 and
- * contract.py:48-53): every pointer is DEVICE memory owned by the caller; entry points neither allocate
- * nor free (scratch is a caller buffer sized by the matching *_workspace_bytes query, as the reference
- * requests scratch as an extra output, contract.py:16-17); work is enqueued on `stream` (a cudaStream_t)
- * without host synchronisation; absent optional tensors are NULL.  Every function returns CFK_OK or a
- * negative status and never throws or aborts.  dtype tags: CFK_F32, CFK_BF16, CFK_E4M3.
+ * contract.py:48-53): every pointer is DEVICE memory owned by the caller; entry points take their scratch
+ * from the caller (a buffer sized by the matching *_workspace_bytes query, as the reference requests
+ * scratch as an extra output, contract.py:16-17); work is enqueued on `stream` (a cudaStream_t) without host
+ * synchronisation; absent optional tensors are NULL.  Every function returns CFK_OK or a negative status
+ * and never throws or aborts.  dtype tags: CFK_F32, CFK_BF16, CFK_E4M3.
+ *
+ * One process may drive several devices: every entry works on the current device.  The one allocation the
+ * library makes is a 16-byte status word (with a 4-byte pinned host mirror) per device, on the first call of
+ * any tensor-core entry on that device: make that call before any stream capture is begun there.
+ *
+ * Timeouts: every device-side wait is bounded.  A kernel whose wait runs out records an id in the status
+ * word and returns; from then on kernels of this library return at once WITHOUT writing their outputs, and
+ * every entry point answers CFK_ERR_DEVICE_WAIT, until cfk_last_device_status(1) has read and cleared the
+ * word.  The call during which the wait ran out may itself have returned CFK_OK (the work is asynchronous):
+ * outputs produced since the last clean read of the status word are valid only if the next read is 0.
  *
  * Citations name the reference interface each entry replaces (paths inside mirditalab/colabfold-kernels).
  */
@@ -48,6 +58,11 @@ CFK_API const char* cfk_version(void);
  * handlers report through XLA's FFI error object). */
 CFK_API int cfk_last_device_status(int reset);
 
+/* Self-test of the bounded waits: one thread block waits `limit_clocks` (at most 2^24) GPU clocks on a
+ * barrier that nothing arrives on, records `code` (> 0) in the status word and returns; nothing spins past
+ * the limit and nothing traps.  cfk_last_device_status then reports `code`.  No reference counterpart. */
+CFK_API int cfk_debug_wait_timeout(int64_t limit_clocks, int code, void* stream);
+
 /* Number of kernels this library has launched in this process (optionally reset to zero): lets a caller
  * check that its work ran here and not in a fallback.  No reference counterpart. */
 CFK_API long long cfk_launch_count(int reset);
@@ -86,7 +101,7 @@ CFK_API int cfk_layer_norm_bwd_static(const void* x, const float* scale, const v
  * out = softmax_k(scale * q.k + bias[h,q,k], masked keys -> finite floor) . v, per (batch n, head h).
  * q [n,h,sq,d] ('heads') or [n,sq,h,d] (seq_major); k, v likewise with sk; bias [h,sq,sk] in `dtype` or NULL;
  * kmask [n,sk] uint8 (0 = masked); out in q's layout and dtype; lse [n,h,sq] fp32 (log2 domain) or NULL.
- * dtype CFK_BF16 (tcgen05 path when d is 16/32/64 and sk % 8 == 0, else the fp32-math path) or CFK_F32.
+ * dtype CFK_BF16 (tcgen05 path when d == 32 and sk % 8 == 0, else the fp32-math path) or CFK_F32.
  * Replaces tri_flash / pallas_attention's kernel call, tri_flash.py:242-290,452-478 (FFI: volta.py:100-115). */
 CFK_API int cfk_attention_fwd(const void* q, const void* k, const void* v, const void* bias, const uint8_t* kmask, void* out,
                       float* lse, int n, int h, int sq, int sk, int d, int dtype, int seq_major, float scale,
