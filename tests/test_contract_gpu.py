@@ -68,7 +68,7 @@ def test_outer_product_mean_matches_oracle(s, r):
   ref = O.ref_opm_deep(left, right, mask, w, bias, res)
   got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda())
   assert ops.device_status() == 0
-  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
+  assert O.rel_err(got.cpu().float(), ref) <= 2e-2
   # row-sharded use: a slice of the left rows against all of the right
   part = ops.outer_product_mean(left[:, 2:7].cuda(), right.cuda(), mask[:, 2:7].cuda(), mask.cuda(), w.cuda(), bias.cuda(),
                                 residual=res[2:7].cuda())
@@ -88,8 +88,8 @@ def test_shallow_opm_forms_match_the_reference_fixtures(golden):
   assert callable(sel)
   got = sel(bf16(g["left"]), bf16(g["right"]), bf16(g["w"]))
   ref = O.ref_opm_outer(bf16(g["left"]).cpu(), bf16(g["right"]).cpu(), bf16(g["w"]).cpu())
-  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
-  assert O.rel_err(got.cpu().float(), torch.from_numpy(np.asarray(g["out"], dtype=np.float32))) <= 5e-2
+  assert O.rel_err(got.cpu().float(), ref) <= 2e-2
+  assert O.rel_err(got.cpu().float(), torch.from_numpy(np.asarray(g["out"], dtype=np.float32))) <= 2e-2
   g = golden("opm_update")
   k = g["lhs"].shape[1]
   f = g["t"].shape[2]
@@ -99,7 +99,7 @@ def test_shallow_opm_forms_match_the_reference_fixtures(golden):
             bf16(g["residual"]))
   ref = O.ref_opm_update(bf16(g["lhs"]).cpu(), bf16(g["t"]).cpu(), bf16(g["bias"]).cpu(),
                          torch.from_numpy(np.asarray(g["norm"], dtype=np.float32)), bf16(g["residual"]).cpu())
-  assert O.rel_err(got.cpu().float(), ref) <= 3e-2
+  assert O.rel_err(got.cpu().float(), ref) <= 2e-2
   assert fused_ops.opm_outer(cfg, torch.bfloat16, 12, c, d, f) is None       # not 16 rows: the caller's own path
   assert fused_ops.opm_update(cfg, torch.bfloat16, 40, 128) is None           # K not a multiple of 32
   assert ops.device_status() == 0
@@ -149,7 +149,7 @@ def test_outer_product_mean_e4m3_opt_in():
   assert ops.device_status() == 0 and torch.isfinite(got).all()
   l8, r8 = O.e4m3(left).float(), O.e4m3(right).float()
   assert float(l8[0, 0, 0]) == 448.0
-  assert O.rel_err(got.cpu().float(), O.ref_opm_deep(l8, r8, mask, w, bias, res)) <= 3e-2
+  assert O.rel_err(got.cpu().float(), O.ref_opm_deep(l8, r8, mask, w, bias, res)) <= 2e-2
   left[0, 0, 0] = 0.5
   got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda(), fp8=True)
   assert O.rel_err(got.cpu().float(), O.ref_opm_deep(left, right, mask, w, bias, res)) <= 6e-2

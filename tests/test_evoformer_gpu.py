@@ -1,5 +1,5 @@
 """One Evoformer block on the GPU (every op a kernel of the library except the transitions' GEMMs) against the
-same composition on the CPU oracle.  bf16 through nine residual updates: rel <= 5e-2 on both representations."""
+same composition on the CPU oracle.  bf16 through nine residual updates: rel <= 2e-2 on both representations."""
 import pytest
 import torch
 
@@ -26,8 +26,8 @@ def test_block_matches_oracle(s, r):
   m, p = evoformer.block(evoformer.cuda_kernels(), msa.cuda(), pair.cuda(), msa_mask.cuda(), pair_mask.cuda(),
                          to_cuda(params))
   assert ops.device_status() == 0
-  assert O.rel_err(m.cpu().float(), ref_m) <= 5e-2
-  assert O.rel_err(p.cpu().float(), ref_p) <= 5e-2
+  assert O.rel_err(m.cpu().float(), ref_m) <= 2e-2
+  assert O.rel_err(p.cpu().float(), ref_p) <= 2e-2
 
 
 def test_block_with_e4m3_triangle_operands():

@@ -8,7 +8,7 @@ import torch
 import oracle as O
 
 pytestmark = pytest.mark.gpu
-TOL = 3e-2  # the reference's bound for the fused projections (tests/test_af2_fused_kernels.py:22)
+TOL = 2e-2  # bf16 bound of this build (the reference's own bound for these ops is 3e-2, tests/test_af2_fused_kernels.py:22)
 bf = torch.bfloat16
 
 
