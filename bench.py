@@ -51,6 +51,14 @@ def peaks():
   return 1590.0, 6650.0, "fallback"
 
 
+def sustained_peak():
+  """Dense bf16 TFLOP/s of a seconds-long GEMM loop under the power cap: the denominator for a whole block."""
+  path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+  if os.path.exists(path):
+    return float(json.load(open(path)).get("bf16_tflops_sustained", 1400.0))
+  return 1400.0
+
+
 class ClockSampler(threading.Thread):
   """nvidia-smi clocks and throttle reasons every 200 ms while the timed region runs."""
 
@@ -82,9 +90,12 @@ class ClockSampler(threading.Thread):
 
 
 def cpu_arm(steps, warmup, sample_b=32):
-  """The CPU oracle on a bounded sample (sample_b batch rows of the same heads/seq/head_dim), all host threads."""
+  """The CPU oracle on a bounded sample (sample_b batch rows of the same heads/seq/head_dim) on every host core.
+  The thread count is set here: under torch.distributed.run the environment pins OMP_NUM_THREADS to 1."""
   import torch
   import oracle as O
+  cores = os.cpu_count() or 1
+  torch.set_num_threads(cores)
   g = torch.Generator().manual_seed(0)
   q, k, v, do = (torch.randn(sample_b, H, S, D, generator=g) for _ in range(4))
   bias = torch.randn(H, S, S, generator=g)
@@ -96,17 +107,19 @@ def cpu_arm(steps, warmup, sample_b=32):
     lse = O.ref_attn_lse(q, k, bias, kmask, scale)
     return O.ref_attn_bwd(q, k, v, bias, kmask, out, do, lse, scale)
 
-  for _ in range(max(1, min(warmup, 1))):
+  n_warm, n_timed = max(1, min(warmup, 1)), max(1, min(steps, 3))
+  for _ in range(n_warm):
     step()
   times = []
-  for _ in range(max(1, min(steps, 3))):
+  for _ in range(n_timed):
     t0 = time.perf_counter()
     step()
     times.append(time.perf_counter() - t0)
   sec = sorted(times)[len(times) // 2]
   return {"value": flops(sample_b) / sec / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
           "sample": f"{sample_b} of {B} batch rows (h={H}, s={S}, d={D}), fp32 PyTorch-CPU port of ref_attn + flash backward, "
-                    f"median of {len(times)}", "ms_per_sample": sec * 1e3}
+                    f"median of {n_timed} timed samples after {n_warm} warm-up",
+          "ms_per_sample": sec * 1e3, "steps_timed": n_timed, "warmup_run": n_warm, "sample_b": sample_b}
 
 
 def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False, fp8_attention=False, graph=True):
@@ -159,6 +172,35 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   return float(ms), launch
 
 
+def block_matches_single_gpu(world, rank, dev, n_seq=64, n_res=256):
+  """The row-sharded block against the one-GPU block on the same inputs at a small size: every rank runs its shard,
+  rank 0 also runs the whole block and compares (max-abs error over max-abs value, both representations)."""
+  import torch
+  import torch.distributed as dist
+  from colabfold_kernels import evoformer
+  bf = torch.bfloat16
+  g = torch.Generator().manual_seed(7)
+  msa = torch.randn(n_seq, n_res, 256, generator=g).to(bf).to(dev)
+  pair = torch.randn(n_res, n_res, 128, generator=g).to(bf).to(dev)
+  msa_mask = (torch.rand(n_seq, n_res, generator=g) < 0.95).float().to(dev)
+  pair_mask = (torch.rand(n_res, n_res, generator=g) < 0.95).float().to(dev)
+  params = evoformer.init_params(device=dev)
+  K = evoformer.cuda_kernels()
+  blk = evoformer.ShardedBlock(K, params)
+  m_l, p_l = blk(msa[blk.shard(n_seq)].contiguous(), pair[blk.shard(n_res)].contiguous(), msa_mask, pair_mask)
+  m_all = torch.empty((world,) + tuple(m_l.shape), dtype=bf, device=dev)
+  p_all = torch.empty((world,) + tuple(p_l.shape), dtype=bf, device=dev)
+  dist.all_gather_into_tensor(m_all, m_l.contiguous())
+  dist.all_gather_into_tensor(p_all, p_l.contiguous())
+  err = None
+  if rank == 0:
+    m1, p1 = evoformer.block(K, msa, pair, msa_mask, pair_mask, params)
+    rel = lambda a, b: float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-3))
+    err = max(rel(m_all.reshape(m1.shape), m1), rel(p_all.reshape(p1.shape), p1))
+  dist.barrier()
+  return err
+
+
 def main():
   ap = argparse.ArgumentParser()
   ap.add_argument("--gpus", type=int, default=1)
@@ -171,6 +213,11 @@ def main():
   ap.add_argument("--batch", type=int, default=B, help="batch rows per GPU (smaller values are for profiler captures only)")
   args = ap.parse_args()
   globals()["B"] = args.batch
+  # NCCL writes its log (NCCL_DEBUG) to file descriptor 1.  The JSON line must stand alone on stdout, so the process's
+  # descriptor 1 is pointed at stderr and the line goes to a private copy of the original stdout.
+  sys.stdout.flush()
+  real_stdout = os.fdopen(os.dup(1), "w")
+  os.dup2(2, 1)
   rank = int(os.environ.get("RANK", "0"))
   world = int(os.environ.get("WORLD_SIZE", "1"))
   local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -179,13 +226,18 @@ def main():
     if rank != 0:
       return
     cb = cpu_arm(args.steps, args.warmup)
+    # `steps` / `warmup` are what was run (the sample is bounded, so at most three timed samples); ms_per_step is the
+    # estimate for the whole workload: the time of the sample times B / sample rows (the work is linear in the batch)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_sample"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload(), "note": "reference's jnp path needs JAX (absent): CPU port of it, bounded sample"},
+            "steps": cb["steps_timed"], "warmup": cb["warmup_run"], "ms_per_step": cb["ms_per_sample"] * B / cb["sample_b"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload(), "ms_per_sample": cb["ms_per_sample"], "sample_rows": cb["sample_b"],
+                       "steps_requested": args.steps,
+                       "note": "reference's jnp path needs JAX (absent): CPU port of it; each timed sample is "
+                               f"{cb['sample_b']} of the {B} batch rows and ms_per_step scales it to the whole batch"},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    print(json.dumps(line), file=real_stdout, flush=True)
     return
 
   import torch
@@ -196,8 +248,6 @@ def main():
   torch.cuda.set_device(local_rank)
   dev = torch.device("cuda", local_rank)
   if world > 1:
-    # NCCL writes its log, the version banner of the VERSION / WARN levels included, to stdout in front of the JSON line
-    os.environ.pop("NCCL_DEBUG", None)
     dist.init_process_group("nccl", device_id=dev)
   lib = _lib.load()
   bf = torch.bfloat16
@@ -319,9 +369,14 @@ def main():
   del ref_out, ref_lse, ref_dk
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-  block_ms = block_f8_ms = block_f8a_ms = block_launch = None
+  block_ms = block_f8_ms = block_f8a_ms = block_launch = block_1gpu_ms = block_err = None
   if args.block:
     graph = args.block_graph != 0
+    if world > 1:
+      block_err = block_matches_single_gpu(world, rank, dev)
+      if rank == 0:  # the same block on this GPU alone: the denominator of the strong-scaling figure
+        block_1gpu_ms, _ = evoformer_block_ms(1, 0, dev, graph=graph)
+      dist.barrier()
     block_ms, block_launch = evoformer_block_ms(world, rank, dev, graph=graph)
     block_f8_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, graph=graph)
     block_f8a_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, fp8_attention=True, graph=graph)
@@ -332,14 +387,21 @@ def main():
 
   if rank == 0:
     peak_tf, _, peak_kind = peaks()
+    sustained_tf = sustained_peak()
     fwd = sorted(fwd_ms)[len(fwd_ms) // 2]
     bwd = sorted(bwd_ms)[len(bwd_ms) // 2]
     dominant, dom_ms, dom_flops = ("attention_bwd", bwd, 10.0 * B * H * S * S * D) if bwd >= fwd else \
                                   ("attention_fwd", fwd, 4.0 * B * H * S * S * D)
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-    # DRAM bytes of one launch from the ncu captures of the b=96 case (profiles/attention_*_sm100__b96_h8_s1024_d32.md),
-    # scaled by batch: every term but the 16.8 MB bias tile grows with the batch
-    traffic = (862.02e6 if dominant == "attention_bwd" else 235.96e6) * B / 96.0
+    # DRAM bytes of one launch: the ncu capture of a small batch of the same shape, listed by kernel in the capture
+    # table beside the profiles, scaled by batch (every term but the 16.8 MB bias tile grows with it); null without it
+    traffic = traffic_src = None
+    try:
+      cap = json.load(open(os.path.join(ROOT, "profiles", "attention_dram_traffic.json")))[dominant]
+      traffic = float(cap["dram_bytes_per_launch"]) * B / float(cap["batch"])
+      traffic_src = f"ncu capture of {cap['kernel']} at {cap['capture']}, scaled by batch {B}/{cap['batch']}"
+    except Exception:
+      pass
     line = {
         "metric": METRIC, "value": flops(B) * world / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -356,14 +418,25 @@ def main():
                 "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms), "chunks": n_chunks,
                 "matches_resident_step": e2e_ok},
         "gpu_launches": int(launches),
+        "block_ms": block_ms,
+        "block_roofline": None if block_ms is None else {
+            "bound": "tensor", "flop": 6.138e12, "achieved": 6.138e12 / (block_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "peak": sustained_tf * world, "frac": 6.138e12 / (block_ms * 1e-3) / 1e12 / (sustained_tf * world),
+            "peak_source": f"{peak_kind} sustained bf16 x {world} GPUs"},
+        "block_speedup_vs_1gpu": None if not block_1gpu_ms else block_1gpu_ms / block_ms,
+        "block_ms_1gpu": block_1gpu_ms,
+        "block_matches_single_gpu": None if block_err is None else {"max_rel_err": block_err, "ok": block_err <= 2e-2,
+                                                                    "n_seq": 64, "n_res": 256},
         "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf, "traffic": traffic, "traffic_unit": "bytes per launch (DRAM read + write)",
+                     "traffic_source": traffic_src,
                      "peak_source": f"{peak_kind} burst bf16"},
         "clocks": sampler.summary(),
     }
     if world == 1:  # the CPU arm is reported at N = 1 only
-      line["cpu_baseline"] = {k: v for k, v in cpu_arm(3, 1).items() if k != "ms_per_sample"}
-    print(json.dumps(line))
+      cb = cpu_arm(3, 1)
+      line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), file=real_stdout, flush=True)
   if world > 1:
     dist.destroy_process_group()
 
