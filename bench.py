@@ -186,7 +186,7 @@ def block_matches_single_gpu(world, rank, dev, n_seq=64, n_res=256):
   pair_mask = (torch.rand(n_res, n_res, generator=g) < 0.95).float().to(dev)
   params = evoformer.init_params(device=dev)
   K = evoformer.cuda_kernels()
-  blk = evoformer.ShardedBlock(K, params)
+  blk = evoformer.ShardedBlock(K, params, exchange_triangle=True)  # the form the large ranks counts take
   m_l, p_l = blk(msa[blk.shard(n_seq)].contiguous(), pair[blk.shard(n_res)].contiguous(), msa_mask, pair_mask)
   m_all = torch.empty((world,) + tuple(m_l.shape), dtype=bf, device=dev)
   p_all = torch.empty((world,) + tuple(p_l.shape), dtype=bf, device=dev)

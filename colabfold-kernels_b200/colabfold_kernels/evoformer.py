@@ -72,6 +72,7 @@ def cuda_kernels():
       ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,
       opm_projection=ops.opm_projection, outer_product_mean=ops.outer_product_mean,
       ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, contract_gathered=ops.contract_gathered,
+      contract_exchanged=ops.contract_exchanged,
       trimul_epilogue=ops.trimul_epilogue,
       transition=transition)
 
@@ -142,14 +143,23 @@ def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_atten
 
 
 # ------------------------------------------------------------------------------------------ sharded over P ranks
+class ShardError(ValueError):
+  """The shards handed to the sharded block do not fit its partitioning (raised before anything is launched)."""
+
+
+class CollectiveTimeout(RuntimeError):
+  """A collective of the sharded block did not complete in time (a peer is missing or stuck)."""
+
+
 class ShardedBlock:
   """The same block with the MSA sharded over sequences and the pair over rows, one rank per GPU.
 
   Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
   replicated.  s and r must be divisible by the world size."""
 
-  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False, fp8_opm=False):
+  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False, fp8_opm=False, exchange_triangle=None):
     import torch.distributed as dist
+    self.exchange_triangle = exchange_triangle  # None: by rank count; True / False: force the exchanged / gathered form
     self.K, self.params, self.dist, self.group = K, params, dist, group
     self.f8 = {"fp8": True} if fp8_trimul else {}  # e4m3 triangle operands: the gathered operand is half the bytes
     self.fa = {"fp8": True} if fp8_attention else {}  # e4m3 q and k in the attentions
@@ -191,11 +201,88 @@ class ShardedBlock:
       return self.K.contract_gathered(a, self.gather(b_local, 0).view((self.P,) + tuple(b_local.shape)))
     return self.K.contract(a, self.gather(b_local, 1))
 
+  def exchange(self, x):
+    """All-to-all of x [P, ...] along its leading axis (part p goes to rank p), no re-layout on either side."""
+    recv = torch.empty_like(x)
+    if x.element_size() == 1:  # e4m3 operands travel as bytes
+      self.dist.all_to_all_single(recv.view(torch.uint8), x.view(torch.uint8), group=self.group)
+    else:
+      self.dist.all_to_all_single(recv, x, group=self.group)
+    return recv
+
+  def triangle_product(self, a, b, split_k):
+    """x_cm [c, rows/P, r] of a triangle multiplication from this rank's channel-major operands, or None when the
+    shard sizes do not take the exchanged form.  Instead of gathering the right operand of every channel (P - 1 parts
+    of [c, r/P, r] received per rank), the ranks swap to channel shards: an all-to-all of each operand over the
+    channel axis, the contraction of c/P whole channels, and an all-to-all of the product back to row shards.  Each
+    moves (P - 1)/P of one [c, r/P, r] tensor; the operands leave the projection kernel and the product leaves the
+    contraction kernel in the layout the all-to-all sends, and what arrives is read in place.
+    split_k False (outgoing edges): a, b [c, r/P, r], this rank's rows.  True (incoming edges): a, b [c, r, r/P], this
+    rank's slice of the contracted axis."""
+    P = self.P
+    c = a.shape[0]
+    rows, k_local = (a.shape[1], a.shape[2]) if split_k else (a.shape[1] * P, a.shape[2])
+    unit = 128 // a.element_size()  # elements of a 128-byte slice
+    if c % P or rows % (128 * P) or (split_k and k_local % unit) or not hasattr(self.K, "contract_exchanged"):
+      return None
+    if not self.exchange_triangle if self.exchange_triangle is not None else P < 4:
+      return None  # three all-to-alls move 3 (P - 1) / P operand shards, the all-gather P - 1: a gain from 4 ranks on
+    a, b = a.contiguous(), b.contiguous()
+    ap = self.exchange(a.view((P, c // P) + tuple(a.shape[1:])))
+    bp = self.exchange(b.view((P, c // P) + tuple(b.shape[1:])))
+    out = self.exchange(self.K.contract_exchanged(ap, bp, split_k=split_k))  # [P, c/P, rows/P, r] = [c, rows/P, r]
+    return out.view(c, out.shape[2], out.shape[3])
+
   def shard(self, n):
     step = n // self.P
     return slice(self.rank * step, (self.rank + 1) * step)
 
+  def validate(self, msa_s, pair_r, msa_mask, pair_mask, across_ranks=False):
+    """Shape checks of one call's arguments; raises ShardError.  across_ranks also compares the sizes with every other
+    rank's (one small all-reduce: call it outside a CUDA-graph capture)."""
+    P = self.P
+    if msa_mask.ndim != 2 or pair_mask.ndim != 2 or pair_mask.shape[0] != pair_mask.shape[1]:
+      raise ShardError(f"masks must be [s, r] and [r, r], got {tuple(msa_mask.shape)} and {tuple(pair_mask.shape)}")
+    s, r = msa_mask.shape
+    if pair_mask.shape[0] != r:
+      raise ShardError(f"msa_mask has {r} residues, pair_mask {pair_mask.shape[0]}")
+    if s % P or r % P:
+      raise ShardError(f"n_seq = {s} and n_res = {r} must both be divisible by the {P} ranks")
+    if msa_s.ndim != 3 or tuple(msa_s.shape[:2]) != (s // P, r):
+      raise ShardError(f"msa shard must be [n_seq / P, n_res, c] = [{s // P}, {r}, c], got {tuple(msa_s.shape)}")
+    if pair_r.ndim != 3 or tuple(pair_r.shape[:2]) != (r // P, r):
+      raise ShardError(f"pair shard must be [n_res / P, n_res, c] = [{r // P}, {r}, c], got {tuple(pair_r.shape)}")
+    if across_ranks:
+      sizes = torch.tensor([s, r, msa_s.shape[2], pair_r.shape[2]], dtype=torch.int64, device=msa_s.device)
+      lo, hi = sizes.clone(), sizes.clone()
+      self.guarded(lambda: (self.dist.all_reduce(lo, op=self.dist.ReduceOp.MIN, group=self.group),
+                            self.dist.all_reduce(hi, op=self.dist.ReduceOp.MAX, group=self.group)))
+      if not torch.equal(lo.cpu(), hi.cpu()):
+        raise ShardError(f"ranks disagree on (n_seq, n_res, c_m, c_z): min {lo.tolist()}, max {hi.tolist()}")
+
+  def guarded(self, fn, timeout_s=60.0):
+    """Run fn() (which enqueues collectives) under a host-side watchdog: an error the process group raises (its own
+    timeout when a peer never joins, a peer that went away) and device work that has not finished after timeout_s
+    both become CollectiveTimeout, so the caller sees an error instead of a stuck rank."""
+    import time
+    try:
+      out = fn()
+      if torch.cuda.is_available() and torch.cuda.is_initialized():
+        done = torch.cuda.Event()
+        done.record()
+        deadline = time.monotonic() + timeout_s
+        while not done.query():
+          if time.monotonic() > deadline:
+            raise CollectiveTimeout(f"device work of rank {self.rank} still pending after {timeout_s:.0f} s")
+          time.sleep(0.001)
+      return out
+    except CollectiveTimeout:
+      raise
+    except (RuntimeError, self.dist.DistBackendError) as e:
+      raise CollectiveTimeout(f"collective failed on rank {self.rank}: {e}") from e
+
   def __call__(self, msa_s, pair_r, msa_mask, pair_mask):
+    self.validate(msa_s, pair_r, msa_mask, pair_mask)
     K, prm, d = self.K, self.params, self.params["d_head"]
     s, r = msa_mask.shape
     ss, rs = self.shard(s), self.shard(r)
@@ -217,13 +304,22 @@ class ShardedBlock:
     t = prm["tri_out"]
     l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
                                  pair_mask[rs].contiguous().to(pair_r.dtype), **self.f8)
-    pair_r = triangle_update(K, pair_r, self.contract_all(l, rr), t)
-    # 6 incoming edges: operands come from the column-sharded pair, read transposed
+    x_cm = self.triangle_product(l, rr, False)
+    pair_r = triangle_update(K, pair_r, x_cm if x_cm is not None else self.contract_all(l, rr), t)
+    # 6 incoming edges: out[i, j] = sum_k r[k, i] l[k, j].  Read transposed, this rank's pair rows give every (i, j)'s
+    # operands for its own k: a slice of the contracted axis
     t = prm["tri_in"]
-    pair_c = self.rows_to_cols(pair_r)
-    l, rr = K.ln_gated_dual_proj(pair_c, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
-                                 pair_mask[:, rs].contiguous().to(pair_r.dtype), transpose=True, **self.f8)
-    pair_r = triangle_update(K, pair_r, self.contract_all(rr, l), t)
+    l, rr, x_cm = None, None, None
+    if r % (128 * self.P) == 0 and (self.exchange_triangle if self.exchange_triangle is not None else self.P >= 4):
+      l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
+                                   pair_mask[rs].contiguous().to(pair_r.dtype), transpose=True, **self.f8)
+      x_cm = self.triangle_product(rr, l, True)
+    if x_cm is None:  # shard sizes outside the exchanged form: operands from the column-sharded pair, gathered
+      pair_c = self.rows_to_cols(pair_r)
+      l, rr = K.ln_gated_dual_proj(pair_c, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
+                                   pair_mask[:, rs].contiguous().to(pair_r.dtype), transpose=True, **self.f8)
+      x_cm = self.contract_all(rr, l)
+    pair_r = triangle_update(K, pair_r, x_cm, t)
     # 7 triangle attention, starting node
     bias = self.gather(head_bias(K, pair_r, prm["tri_attn_start"]), 1)
     pair_r = attend(K, pair_r, prm["tri_attn_start"], bias, pm[rs].contiguous(), False, d, **self.fa)

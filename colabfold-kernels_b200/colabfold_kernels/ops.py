@@ -181,6 +181,24 @@ def contract_gathered(a, b_parts, alpha=1.0):
   return out
 
 
+def contract_exchanged(a_parts, b_parts, split_k=False, alpha=1.0, out=None):
+  """The contraction between two all-to-alls over the channel axis.  split_k False: a_parts [P, c, i/P, k],
+  b_parts [P, c, j/P, k]; True: a_parts [P, c, i, k/P], b_parts [P, c, j, k/P] -> [P, c, i/P, j] bf16, the send buffer
+  of the all-to-all back to row shards."""
+  a_parts, b_parts = _c(a_parts), _c(b_parts)
+  parts, c = a_parts.shape[0], a_parts.shape[1]
+  if split_k:
+    i, j, k = a_parts.shape[2], b_parts.shape[2], a_parts.shape[3] * parts
+  else:
+    i, j, k = a_parts.shape[2] * parts, b_parts.shape[2] * parts, a_parts.shape[3]
+  if out is None:
+    out = torch.empty((parts, c, i // parts, j), dtype=torch.bfloat16, device=a_parts.device)
+  with torch.cuda.device(a_parts.device):
+    _lib.call("cfk_contract_exchanged", _ptr(a_parts), _ptr(b_parts), _ptr(out), c, i, j, k, tag(a_parts.dtype), float(alpha),
+              parts, int(split_k), _stream())
+  return out
+
+
 # ------------------------------------------------------------------------------------------ projection family
 def _f32(t):
   return _c(t.float())

@@ -35,6 +35,11 @@ struct ContractParams {
   int* status;
   int opm;              // 1: rows are (i, 32 channels), columns (j, 32 channels); the product is stored as [i, j, 32, 32]
   int part_rows;        // > 0: b is [parts, C, part_rows, K] (an all-gather's output); a multiple of 128
+  // Operands and product as an all-to-all over the channel axis leaves / wants them (4-D tensor maps
+  // {x, rows, c, part}).  mode 0: plain 3-D; 1: split by rows, [parts, C, rows / parts, X] with `div` rows per part
+  // (a multiple of 128); 2: split along K, [parts, C, rows, K / parts] with `div` elements per part (a multiple of
+  // the 128-byte slice).  The product only takes modes 0 and 1.
+  int a_mode, a_div, b_mode, b_div, o_div;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,8 +99,19 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
           ok = mbar_wait_deadline(&empty[st], ((it / kStages) & 1) ^ 1);
           if (!ok) { report_timeout(prm.status, 401); break; }
           mbar_arrive_expect_tx(&full[st], kSliceA + kSliceB);
-          tma_load_3d(smem + kOffA + st * kSliceA, &tm_a, &full[st], s * prm.k_per_slice, i0, c);
-          if (prm.part_rows > 0) {
+          const int kx = s * prm.k_per_slice;
+          if (prm.a_mode == 1)
+            tma_load_4d(smem + kOffA + st * kSliceA, &tm_a, &full[st], kx, i0 % prm.a_div, c, i0 / prm.a_div);
+          else if (prm.a_mode == 2)
+            tma_load_4d(smem + kOffA + st * kSliceA, &tm_a, &full[st], kx % prm.a_div, i0, c, kx / prm.a_div);
+          else
+            tma_load_3d(smem + kOffA + st * kSliceA, &tm_a, &full[st], kx, i0, c);
+          if (prm.b_mode == 2) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(smem + kOffB + st * kSliceB + h * (128 * 128), &tm_b, &full[st], kx % prm.b_div, j0 + h * 128, c,
+                          kx / prm.b_div);
+          } else if (prm.part_rows > 0) {
             // rows j0 .. j0+255 of the gathered operand: two 128-row boxes, each inside one part
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -188,6 +204,9 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 #pragma unroll
             for (int sub = 0; sub < 4; ++sub)
               tma_store_4d(&tm_o, stage + sub * (kTM * 64), 0, 0, (j0 + half * 128) / 32 + sub, i0 / 32);
+          } else if (prm.o_div > 0) {
+            tma_store_4d(&tm_o, stage, j0 + half * 128, i0 % prm.o_div, c, i0 / prm.o_div);
+            tma_store_4d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0 % prm.o_div, c, i0 / prm.o_div);
           } else {
             tma_store_3d(&tm_o, stage, j0 + half * 128, i0, c);
             tma_store_3d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0, c);
@@ -217,8 +236,10 @@ using namespace cfk;
 namespace {
 // opm_ri > 0: a is [(opm_ri x 32), k], b [(opm_rj x 32), k] and the product is stored as out[opm_ri, opm_rj, 32, 32]
 // parts > 1: b is [parts, c, j / parts, k], the layout an all-gather of per-rank [c, j / parts, k] operands leaves
+// xmode / xparts (exchanged form): mode 1 = operands split by rows over xparts, mode 2 = split along K; the product
+// is then stored split by rows, [xparts, C, I / xparts, J]
 int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha, int opm_ri,
-                  int opm_rj, int parts, void* stream) {
+                  int opm_rj, int parts, void* stream, int xmode = 0, int xparts = 1) {
   if (a == nullptr || b == nullptr || out == nullptr) return CFK_ERR_NULL;
   if (c <= 0 || i <= 0 || j <= 0 || k <= 0) return CFK_ERR_SHAPE;
   if (dtype != CFK_BF16 && dtype != CFK_E4M3) return CFK_ERR_DTYPE;
@@ -227,6 +248,37 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
   if ((int64_t(k) * es) % 16 != 0 || j % 8 != 0) return CFK_ERR_SHAPE;
   if (!aligned16(a) || !aligned16(b) || !aligned16(out)) return CFK_ERR_ALIGN;
   CUtensorMap ta, tb, to;
+  int a_div = 0, b_div = 0, o_div = 0, part_rows = 0;
+  if (xmode != 0) {
+    const int kps = 128 / es;
+    if (xparts <= 0 || i % xparts != 0 || (i / xparts) % kTM != 0) return CFK_ERR_SHAPE;
+    o_div = i / xparts;
+    if (xmode == 1) {
+      if (j % xparts != 0 || (j / xparts) % 128 != 0) return CFK_ERR_SHAPE;
+      a_div = i / xparts;
+      b_div = j / xparts;
+    } else {
+      if (k % xparts != 0 || (k / xparts) % kps != 0) return CFK_ERR_SHAPE;
+      a_div = b_div = k / xparts;
+    }
+    auto map4 = [&](CUtensorMap* m, const void* base, int rows) {
+      // xmode 1: [parts, C, rows / parts, K]; xmode 2: [parts, C, rows, K / parts]
+      const uint64_t rr = xmode == 1 ? uint64_t(rows / xparts) : uint64_t(rows);
+      const uint64_t kk = xmode == 1 ? uint64_t(k) : uint64_t(k / xparts);
+      uint64_t dims[4] = {kk, rr, uint64_t(c), uint64_t(xparts)};
+      uint64_t str[3] = {kk * es, rr * kk * es, uint64_t(c) * rr * kk * es};
+      uint32_t box[4] = {uint32_t(128 / es), 128, 1, 1};
+      return make_tensor_map(m, base, dtype, 4, dims, str, box, 128);
+    };
+    int rc = map4(&ta, a, i);
+    if (rc == CFK_OK) rc = map4(&tb, b, j);
+    if (rc != CFK_OK) return rc;
+    uint64_t dims[4] = {uint64_t(j), uint64_t(o_div), uint64_t(c), uint64_t(xparts)};
+    uint64_t str[3] = {uint64_t(j) * 2, uint64_t(o_div) * j * 2, uint64_t(c) * o_div * j * 2};
+    uint32_t box[4] = {64, kTM, 1, 1};
+    rc = make_tensor_map(&to, out, CFK_BF16, 4, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  } else {
   {
     uint64_t dims[3] = {uint64_t(k), uint64_t(i), uint64_t(c)};
     uint64_t str[2] = {uint64_t(k) * es, uint64_t(i) * k * es};
@@ -234,7 +286,6 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
     int rc = make_tensor_map(&ta, a, dtype, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  int part_rows = 0;
   if (parts > 1) {
     if (j % parts != 0 || (j / parts) % 128 != 0) return CFK_ERR_SHAPE;
     part_rows = j / parts;
@@ -266,7 +317,10 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
     int rc = make_tensor_map(&to, out, CFK_BF16, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0, part_rows};
+  }
+  // exchanged form: the b boxes of mode 1 go through the gathered operand's path (two 128-row boxes, part = row / div)
+  ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0,
+                     xmode == 1 ? b_div : part_rows, xmode, a_div, xmode == 2 ? 2 : 0, b_div, o_div};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   // a function attribute belongs to the current device: set on every launch, as the other launchers do
   if (cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
@@ -290,6 +344,12 @@ extern "C" int cfk_contract_gathered(const void* a, const void* b, void* out, in
                                      float alpha, int parts, void* stream) {
   if (parts <= 0) return CFK_ERR_SHAPE;
   return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, parts, stream);
+}
+
+extern "C" int cfk_contract_exchanged(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
+                                      float alpha, int parts, int split_k, void* stream) {
+  if (parts <= 0) return CFK_ERR_SHAPE;
+  return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, 1, stream, split_k ? 2 : 1, parts);
 }
 
 extern "C" int cfk_opm_outer_product(const void* a, const void* b, void* out, int ri, int rj, int s, int dtype, void* stream) {

@@ -157,6 +157,17 @@ CFK_API int cfk_contract(const void* a, const void* b, void* out, int c, int i, 
 CFK_API int cfk_contract_gathered(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
                                   float alpha, int parts, void* stream);
 
+/* The same contraction between two all-to-alls over the channel axis (the row-sharded block's triangle
+ * multiplication: each rank contracts C = channels / parts whole channels instead of gathering the right operand).
+ * split_k == 0: a is [parts, C, I/parts, K] and b [parts, C, J/parts, K], what the all-to-all leaves when every rank
+ * sent its rows of all channels; split_k != 0: a is [parts, C, I, K/parts] and b [parts, C, J, K/parts], every rank
+ * having sent its slice of the contracted axis (incoming edges).  The product is stored as [parts, C, I/parts, J]:
+ * the send buffer of the all-to-all back to row shards, no re-layout copy on either side.  I/parts and J/parts
+ * (split_k == 0) must be multiples of 128, K/parts (split_k != 0) a multiple of 64 (bf16) or 128 (e4m3) elements.
+ * No reference counterpart (the reference runs on one device). */
+CFK_API int cfk_contract_exchanged(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
+                                   float alpha, int parts, int split_k, void* stream);
+
 /* The outer product of the outer-product-mean over the MSA depth, for 32-channel projections:
  * out[i, j, c, e] = sum_s a[i*32 + c, s] * b[j*32 + e, s]; a [ri*32, s], b [rj*32, s] in `dtype` (CFK_BF16 or CFK_E4M3),
  * out [ri, rj, 32, 32] bf16 - the layout the output linear of the module contracts over (c, e) without a transposed

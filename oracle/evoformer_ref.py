@@ -36,6 +36,13 @@ def oracle_kernels(dtype=torch.float32):
   def contract_gathered(a, b_parts):  # b_parts [parts, c, j/parts, k]: the right operand as an all-gather leaves it
     return R.ref_contract(a, torch.cat(list(b_parts.unbind(0)), dim=1), dtype)
 
+  def contract_exchanged(a_parts, b_parts, split_k=False):
+    # the operands as an all-to-all over the channel axis leaves them: [P, c, i/P, k] (rows split) or [P, c, i, k/P]
+    # (contracted axis split); the product as the all-to-all back wants it: [P, c, i/P, j]
+    cat = (lambda t: torch.cat(list(t.unbind(0)), dim=2)) if split_k else (lambda t: torch.cat(list(t.unbind(0)), dim=1))
+    out = R.ref_contract(cat(a_parts), cat(b_parts), dtype)
+    return torch.stack(out.chunk(a_parts.shape[0], dim=1), dim=0)
+
   def trimul_epilogue(x_cm, act, ln_scale, ln_offset, wo, bo, wg, bg, residual=None, in_scale=None, in_offset=None,
                       eps=1e-5, add_input=False):
     if in_scale is None:
@@ -49,4 +56,5 @@ def oracle_kernels(dtype=torch.float32):
   return types.SimpleNamespace(ln_projection=ln_projection, packed_attention=packed_attention,
                                output_projection=output_projection, opm_projection=opm_projection,
                                outer_product_mean=outer_product_mean, ln_gated_dual_proj=ln_gated_dual_proj,
-                               contract=contract, contract_gathered=contract_gathered, trimul_epilogue=trimul_epilogue, transition=transition)
+                               contract=contract, contract_gathered=contract_gathered, contract_exchanged=contract_exchanged,
+                               trimul_epilogue=trimul_epilogue, transition=transition)

@@ -153,3 +153,31 @@ def test_outer_product_mean_e4m3_opt_in():
   left[0, 0, 0] = 0.5
   got = ops.outer_product_mean(left.cuda(), right.cuda(), mask.cuda(), mask.cuda(), w.cuda(), bias.cuda(), residual=res.cuda(), fp8=True)
   assert O.rel_err(got.cpu().float(), O.ref_opm_deep(left, right, mask, w, bias, res)) <= 6e-2
+
+
+@pytest.mark.parametrize("split_k", [False, True])
+@pytest.mark.parametrize("dtype", ["bf16", "e4m3"])
+def test_contract_exchanged_reads_and_writes_the_all_to_all_layouts(split_k, dtype):
+  """cfk_contract_exchanged on operands laid out as an all-to-all over the channel axis leaves them (split by rows, or
+  along the contracted axis) must equal cfk_contract on the assembled operands, stored as the all-to-all back wants
+  it ([parts, c, i/parts, j])."""
+  from colabfold_kernels import ops
+  g = torch.Generator().manual_seed(11)
+  parts, c, i, j, k = 4, 3, 512, 1024, 512
+  a = (torch.randn(c, i, k, generator=g) * .5).to(torch.bfloat16).cuda()
+  b = (torch.randn(c, j, k, generator=g) * .5).to(torch.bfloat16).cuda()
+  if dtype == "e4m3":
+    a, b = a.to(torch.float8_e4m3fn), b.to(torch.float8_e4m3fn)
+  whole = ops.contract(a, b)  # [c, i, j]
+  if split_k:
+    ap = torch.stack(a.view(torch.uint8 if dtype == "e4m3" else a.dtype).chunk(parts, dim=2), 0).contiguous()
+    bp = torch.stack(b.view(torch.uint8 if dtype == "e4m3" else b.dtype).chunk(parts, dim=2), 0).contiguous()
+  else:
+    ap = torch.stack(a.view(torch.uint8 if dtype == "e4m3" else a.dtype).chunk(parts, dim=1), 0).contiguous()
+    bp = torch.stack(b.view(torch.uint8 if dtype == "e4m3" else b.dtype).chunk(parts, dim=1), 0).contiguous()
+  if dtype == "e4m3":
+    ap, bp = ap.view(torch.float8_e4m3fn), bp.view(torch.float8_e4m3fn)
+  got = ops.contract_exchanged(ap, bp, split_k=split_k)  # [parts, c, i/parts, j]
+  assert ops.device_status() == 0
+  want = torch.stack(whole.chunk(parts, dim=1), 0)
+  assert torch.equal(got, want)

@@ -19,7 +19,7 @@ def _inputs(s=8, r=16):
   return msa, pair, msa_mask, pair_mask
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, s_r=(8, 16)):
   for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
     sys.path.insert(0, p)
   from colabfold_kernels import evoformer
@@ -27,22 +27,26 @@ def _worker(rank, world, port, out):
   os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
   dist.init_process_group("gloo", rank=rank, world_size=world)
   torch.set_num_threads(2)
-  msa, pair, msa_mask, pair_mask = _inputs()
+  msa, pair, msa_mask, pair_mask = _inputs(*s_r)
   params = evoformer.init_params(dtype=torch.float32, seed=1)
-  blk = evoformer.ShardedBlock(oracle_kernels(), params)
+  blk = evoformer.ShardedBlock(oracle_kernels(), params, exchange_triangle=True)
+  blk.validate(msa[blk.shard(s_r[0])], pair[blk.shard(s_r[1])], msa_mask, pair_mask, across_ranks=True)
   s, r = msa_mask.shape
   m, p = blk(msa[blk.shard(s)].contiguous(), pair[blk.shard(r)].contiguous(), msa_mask, pair_mask)
   torch.save((m, p), os.path.join(out, f"rank{rank}.pt"))
   dist.destroy_process_group()
 
 
-@pytest.mark.timeout(600)
-def test_two_rank_block_matches_single_device(tmp_path):
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("s_r", [(8, 16), (4, 256)])
+def test_two_rank_block_matches_single_device(tmp_path, s_r):
+  """(8, 16): the gathered form of the triangle multiplication; (4, 256): shards of whole 128-row tiles, which take the
+  exchanged form (all-to-all over channels, contraction of whole channels, all-to-all back)."""
   from colabfold_kernels import evoformer
   from oracle.evoformer_ref import oracle_kernels
   world, port = 2, 29611 + os.getpid() % 200
-  mp.spawn(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
-  msa, pair, msa_mask, pair_mask = _inputs()
+  mp.spawn(_worker, args=(world, port, str(tmp_path), s_r), nprocs=world, join=True)
+  msa, pair, msa_mask, pair_mask = _inputs(*s_r)
   params = evoformer.init_params(dtype=torch.float32, seed=1)
   ref_m, ref_p = evoformer.block(oracle_kernels(), msa, pair, msa_mask, pair_mask, params)
   got = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(world)]
@@ -50,3 +54,75 @@ def test_two_rank_block_matches_single_device(tmp_path):
   p = torch.cat([g[1] for g in got], 0)
   assert float((m - ref_m).abs().max()) <= 1e-4 * float(ref_m.abs().max())
   assert float((p - ref_p).abs().max()) <= 1e-4 * float(ref_p.abs().max())
+
+
+def _bad_shard_worker(rank, world, port, out):
+  for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
+    sys.path.insert(0, p)
+  from colabfold_kernels import evoformer
+  from oracle.evoformer_ref import oracle_kernels
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  params = evoformer.init_params(dtype=torch.float32, seed=1)
+  blk = evoformer.ShardedBlock(oracle_kernels(), params)
+  found = []
+  # sizes not divisible by the ranks, a shard of the wrong height, and ranks that disagree on n_res
+  msa, pair, mm, pm = _inputs(7, 16)
+  for args in ((msa[:3], pair[:8], mm, pm), ):
+    try:
+      blk(*args)
+    except evoformer.ShardError as e:
+      found.append(str(e))
+  msa, pair, mm, pm = _inputs(8, 16)
+  try:
+    blk(msa[:4], pair[:5], mm, pm)
+  except evoformer.ShardError as e:
+    found.append(str(e))
+  r = 16 if rank == 0 else 32
+  msa, pair, mm, pm = _inputs(8, r)
+  try:
+    blk.validate(msa[:4], pair[:r // 2], mm, pm, across_ranks=True)
+  except evoformer.ShardError as e:
+    found.append(str(e))
+  torch.save(found, os.path.join(out, f"err{rank}.pt"))
+  dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_shard_errors_are_raised_before_any_work(tmp_path):
+  world, port = 2, 29411 + os.getpid() % 200
+  mp.spawn(_bad_shard_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+  for r in range(world):
+    found = torch.load(os.path.join(tmp_path, f"err{r}.pt"))
+    assert len(found) == 3, found
+    assert "divisible" in found[0] and "pair shard" in found[1] and "disagree" in found[2]
+
+
+def _stuck_worker(rank, world, port, out):
+  import datetime
+  for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
+    sys.path.insert(0, p)
+  from colabfold_kernels import evoformer
+  from oracle.evoformer_ref import oracle_kernels
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+  blk = evoformer.ShardedBlock(oracle_kernels(), evoformer.init_params(dtype=torch.float32, seed=1))
+  result = "peer"
+  if rank == 0:  # rank 1 never joins this collective: the watchdog turns the stuck call into an error
+    x = torch.ones(4)
+    try:
+      blk.guarded(lambda: dist.all_reduce(x))
+      result = "no error"
+    except evoformer.CollectiveTimeout as e:
+      result = "timeout: " + str(e)[:80]
+  torch.save(result, os.path.join(out, f"stuck{rank}.pt"))
+  if rank == 1:
+    import time
+    time.sleep(8)  # stays away from the collective, leaves between steps
+
+
+@pytest.mark.timeout(300)
+def test_missing_peer_becomes_an_error_not_a_hang(tmp_path):
+  world, port = 2, 29211 + os.getpid() % 200
+  mp.spawn(_stuck_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+  assert torch.load(os.path.join(tmp_path, "stuck0.pt")).startswith("timeout")
