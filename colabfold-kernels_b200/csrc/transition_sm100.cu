@@ -5,7 +5,7 @@
 // A persistent CTA walks 128-row tiles of x [M, C].  Per tile:
 //   producer (warp 0)    TMA: the x tile as 64-column K-major atoms; per hidden chunk of 64 columns the weights
 //                        w1[:, chunk] ([C][64], MN-major B) and w2[chunk, :] ([64][C], MN-major B) into two rings
-//   workers (warps 4-7)  LayerNorm of the landed tile in place (thread = row, fp32 statistics, bf16 out: the reference
+//   workers (warps 4-11) LayerNorm of the landed tile in place (thread = row, fp32 statistics, bf16 out: the reference
 //                        rounds the normed tile before the dot, transition.py:76-80); per chunk: acc1 -> + b1 -> relu
 //                        -> bf16 -> H tile in shared memory; per tile: acc2 + b2 (+ x) -> out
 //   issuers (warps 1, 2) per chunk n: acc1[n & 1] = LN(x) w1[:, n]  (C / 16 MMAs of N = 64) from warp 1 and
@@ -19,7 +19,7 @@ namespace {
 
 constexpr int kRowsT = 128;   // rows per tile = TMEM lanes
 constexpr int kHC = 64;       // hidden columns per chunk
-constexpr int kThreadsT = 256;
+constexpr int kThreadsT = 384;   // warps 0-3 control, 4-7 and 8-11 two worker groups
 
 template <int C>
 struct TrCfg {
@@ -29,13 +29,14 @@ struct TrCfg {
   static constexpr int kW2 = 64 * C * 2;                 // w2 chunk: kAtoms atoms of [64 rows][64 columns]
   static constexpr int kH = kRowsT * 128;                // H tile: [128 rows][64 columns]
   static constexpr int kWRing = C == 128 ? 3 : 2;        // ring depth of each weight ring
-  static constexpr int kHBufs = C == 128 ? 2 : 1;        // H buffers
+  static constexpr int kHBufs = 2;                       // H buffers: one per worker group
+  static constexpr int kXBufs = C == 128 ? 2 : 1;        // x tiles in flight
   static constexpr int kOffX = 0;
-  static constexpr int kOffW1 = kOffX + kTileX;
+  static constexpr int kOffW1 = kOffX + kXBufs * kTileX;
   static constexpr int kOffW2 = kOffW1 + kWRing * kW1;
   static constexpr int kOffH = kOffW2 + kWRing * kW2;
   static constexpr int kOffBar = kOffH + kHBufs * kH;
-  static constexpr int kNumBars = 2 + 4 * kWRing + 4 + 4 + 2 + 2;
+  static constexpr int kNumBars = 6 + 4 * kWRing + 4 + 4 + 2 + 2;
   static constexpr int kOffTmem = kOffBar + kNumBars * 8;
   static constexpr int kSmem = kOffTmem + 16 + 1024;
   static constexpr int kColAcc2 = 128;
@@ -63,7 +64,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
                   const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_out,
                   const TrParams prm) {
   using T = TrCfg<C>;
-  constexpr int WR = T::kWRing, HB = T::kHBufs;
+  constexpr int WR = T::kWRing, HB = T::kHBufs, XB = T::kXBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   {
@@ -73,9 +74,10 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     if (s_abort != 0) return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::kOffBar);
-  uint64_t* x_full = bars;             // the x tile has landed
-  uint64_t* x_ready = x_full + 1;      // ... and is normalised (a valid A operand)
-  uint64_t* w1_full = x_ready + 1;     // [WR]
+  uint64_t* x_full = bars;             // [2] the x tile has landed
+  uint64_t* x_ready = x_full + 2;      // [2] ... and is normalised (a valid A operand)
+  uint64_t* x_free = x_ready + 2;      // [2] the tile's result has been read out of the buffer by the TMA store
+  uint64_t* w1_full = x_free + 2;      // [WR]
   uint64_t* w1_empty = w1_full + WR;   // [WR]
   uint64_t* w2_full = w1_empty + WR;   // [WR]
   uint64_t* w2_empty = w2_full + WR;   // [WR]
@@ -94,8 +96,11 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
   const int nchunks = prm.hdim / kHC;
 
   if (threadIdx.x == 0) {
-    mbar_init(x_full, 1);
-    mbar_init(x_ready, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_ready[i], 8);
+      mbar_init(&x_free[i], 1);
+    }
     for (int i = 0; i < WR; ++i) {
       mbar_init(&w1_full[i], 1);
       mbar_init(&w1_empty[i], 1);
@@ -132,14 +137,21 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     if (lane == 0) {
       bool ok = true;
       uint32_t ti = 0, cc = 0;
-      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++ti) {
-        // the x tile is free once every MMA of the tile before has completed and its rows have been re-read
-        ok = mbar_wait_deadline(acc2_empty, (ti & 1) ^ 1);
-        if (!ok) { report_timeout(prm.status, 1101); break; }
-        mbar_arrive_expect_tx(x_full, T::kTileX);
+      // the x tile of local tile index u into its buffer, once the result of the tile that used the buffer before
+      // has been stored out of it
+      auto load_x = [&](uint32_t u, int64_t tile) {
+        const int xb = u % XB;
+        if (!mbar_wait_deadline(&x_free[xb], ((u / XB) & 1) ^ 1)) { report_timeout(prm.status, 1101); return false; }
+        mbar_arrive_expect_tx(&x_full[xb], T::kTileX);
 #pragma unroll
         for (int a = 0; a < T::kAtoms; ++a)
-          tma_load_2d(smem + T::kOffX + a * (kRowsT * 128), &tm_x, x_full, a * 64, int(tile * kRowsT));
+          tma_load_2d(smem + T::kOffX + xb * T::kTileX + a * (kRowsT * 128), &tm_x, &x_full[xb], a * 64, int(tile * kRowsT));
+        return true;
+      };
+      if (int64_t(blockIdx.x) < ntiles) ok = load_x(0, blockIdx.x);
+      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++ti) {
+        const int xb = ti % XB;
+        const int64_t next = tile + gridDim.x;
         for (int n = 0; n < nchunks && ok; ++n, ++cc) {
           const int slot = cc % WR;
           const uint32_t par = ((cc / WR) & 1) ^ 1;
@@ -153,6 +165,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
 #pragma unroll
           for (int a = 0; a < T::kAtoms; ++a)
             tma_load_2d(smem + T::kOffW2 + slot * T::kW2 + a * (64 * 128), &tm_w2, &w2_full[slot], a * 64, n * kHC);
+          // with two buffers the next tile's rows land under this tile's GEMMs
+          if (XB == 2 && n == nchunks / 2 && next < ntiles) ok = load_x(ti + 1, next);
         }
         if (ok && prm.add_input) {
           // the raw rows again, over the normalised tile, for the residual: from L2, under the tile's last GEMMs
@@ -161,8 +175,9 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           mbar_arrive_expect_tx(xraw_full, T::kTileX);
 #pragma unroll
           for (int a = 0; a < T::kAtoms; ++a)
-            tma_load_2d(smem + T::kOffX + a * (kRowsT * 128), &tm_x, xraw_full, a * 64, int(tile * kRowsT));
+            tma_load_2d(smem + T::kOffX + xb * T::kTileX + a * (kRowsT * 128), &tm_x, xraw_full, a * 64, int(tile * kRowsT));
         }
+        if (XB == 1 && ok && next < ntiles) ok = load_x(ti + 1, next);
       }
     }
     __syncwarp();
@@ -180,7 +195,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       const uint32_t h_k = desc_lo(smem_u32(smem + T::kOffH), 16);
       bool ok = true;
       uint32_t ti = 0, c1 = 0, c2 = 0;  // tiles done, chunks whose first / second GEMM has been issued
-      auto gemm1 = [&]() {
+      auto gemm1 = [&](uint32_t xoff) {
         const int slot = c1 % WR, buf = c1 & 1;
         if (!mbar_wait_deadline(&w1_full[slot], (c1 / WR) & 1)) { report_timeout(prm.status, 1201); return false; }
         if (!mbar_wait_deadline(&acc1_empty[buf], ((c1 >> 1) & 1) ^ 1)) { report_timeout(prm.status, 1202); return false; }
@@ -190,7 +205,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         // weight chunk (2048 bytes on)
 #pragma unroll
         for (int kk = 0; kk < C / 16; ++kk)
-          mma_f16_ss2(tmem + buf * kHC, x_k + (kk / 4) * ((kRowsT * 128) >> 4) + (kk % 4) * 2, hi128, b + kk * 128, hi128, idesc1,
+          mma_f16_ss2(tmem + buf * kHC, x_k + xoff + (kk / 4) * ((kRowsT * 128) >> 4) + (kk % 4) * 2, hi128, b + kk * 128, hi128, idesc1,
                       kk > 0);
         mma_commit(&w1_empty[slot]);
         mma_commit(&acc1_full[buf]);
@@ -213,10 +228,11 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       };
       for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++ti) {
         if (warp == 1) {
-          ok = mbar_wait_deadline(x_ready, ti & 1);
+          const int xb = ti % XB;
+          ok = mbar_wait_deadline(&x_ready[xb], (ti / XB) & 1);
           if (!ok) { report_timeout(prm.status, 1205); break; }
           tc_fence_after();
-          for (int n = 0; n < nchunks && ok; ++n) ok = gemm1();
+          for (int n = 0; n < nchunks && ok; ++n) ok = gemm1(xb * (T::kTileX >> 4));
           if (ok) mma_commit(x_dead);
         } else {
           // acc2 of the tile before has been read out
@@ -230,10 +246,17 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     }
     __syncwarp();
   } else if (warp >= 4) {
-    // ------------------------------------------------------------------ workers: thread = row of the tile
+    // ------------------------------------------------------------------ workers: two groups of 128 threads, thread = row
+    // of the tile.  Group g normalises and finally writes column half g of the row and owns the chunks n with
+    // (chunks so far + n) % 2 == g, with them acc1[g] and H[g]: the chunk epilogue is a chain of dependent
+    // instructions per warp, so two warps per scheduler hide what one cannot.
+    const int g = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    // the statistics' partial sums cross the groups through the H buffers, which no MMA reads between two tiles
+    float* red_sum = reinterpret_cast<float*>(smem + T::kOffH);
+    float* red_var = red_sum + 2 * kRowsT;
     bool ok = true;
 #define CFK_TR_WAIT(bar, parity, code)                            \
   if (ok && !mbar_wait_deadline((bar), (parity))) {               \
@@ -242,21 +265,27 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
   }
     uint32_t ti = 0, ce = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++ti) {
-      // ---- LayerNorm of this thread's row, in place (three passes over the 2 C bytes of the row in shared memory)
-      CFK_TR_WAIT(x_full, ti & 1, 1301)
-      uint8_t* xt = smem + T::kOffX;
+      const int xb = ti % XB;
+      uint8_t* xt = smem + T::kOffX + xb * T::kTileX;
+      constexpr int kHalf = C / 16;   // 8-column pieces of this group's half of the row
+      // ---- LayerNorm of the row in place (three passes over this group's C bytes of it in shared memory)
+      CFK_TR_WAIT(&x_full[xb], (ti / XB) & 1, 1301)
       float sum = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < C / 8; ++ch) {
+      for (int i = 0; i < kHalf; ++i) {
+        const int ch = g * kHalf + i;
         const uint4 w = *reinterpret_cast<const uint4*>(xt + (ch / 8) * (kRowsT * 128) + swz_off(row, ch % 8, 128));
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) sum += bf16lo_to_f32(ww[e]) + bf16hi_to_f32(ww[e]);
       }
-      const float mean = sum * (1.0f / C);
+      red_sum[g * kRowsT + row] = sum;
+      named_bar_sync(2, 256);
+      const float mean = (red_sum[row] + red_sum[kRowsT + row]) * (1.0f / C);
       float var = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < C / 8; ++ch) {
+      for (int i = 0; i < kHalf; ++i) {
+        const int ch = g * kHalf + i;
         const uint4 w = *reinterpret_cast<const uint4*>(xt + (ch / 8) * (kRowsT * 128) + swz_off(row, ch % 8, 128));
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -265,9 +294,12 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           var = fmaf(a, a, fmaf(b, b, var));
         }
       }
-      const float rstd = rsqrtf(var * (1.0f / C) + prm.eps);
+      red_var[g * kRowsT + row] = var;
+      named_bar_sync(2, 256);
+      const float rstd = rsqrtf((red_var[row] + red_var[kRowsT + row]) * (1.0f / C) + prm.eps);
 #pragma unroll
-      for (int ch = 0; ch < C / 8; ++ch) {
+      for (int i = 0; i < kHalf; ++i) {
+        const int ch = g * kHalf + i;
         uint4* ptr = reinterpret_cast<uint4*>(xt + (ch / 8) * (kRowsT * 128) + swz_off(row, ch % 8, 128));
         const uint4 w = *ptr;
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
@@ -285,12 +317,14 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         *ptr = make_uint4(y[0], y[1], y[2], y[3]);
       }
       fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(x_ready);
+      // both groups have read the partial sums before a chunk epilogue writes an H buffer over them
+      named_bar_sync(2, 256);
+      if (lane == 0) mbar_arrive(&x_ready[xb]);
 
-      // ---- per hidden chunk: relu(acc1 + b1) as bf16 into the H tile (the second GEMM's A operand)
+      // ---- per hidden chunk of this group: relu(acc1 + b1) as bf16 into the H tile (the second GEMM's A operand)
 #pragma unroll 1
       for (int n = 0; n < nchunks; ++n, ++ce) {
+        if (int(ce & 1) != g) continue;
         const int buf = ce & 1, hb = ce % HB;
         CFK_TR_WAIT(&acc1_full[buf], (ce >> 1) & 1, 1302)
         tc_fence_after();
@@ -331,7 +365,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       if (prm.add_input) CFK_TR_WAIT(xraw_full, ti & 1, 1305)
       tc_fence_after();
 #pragma unroll 1
-      for (int cb = 0; cb < C / 32; ++cb) {
+      for (int i = 0; i < C / 64; ++i) {
+        const int cb = g * (C / 64) + i;
         uint32_t r[32];
         tmem_ld_x32(tmem + lane_addr + T::kColAcc2 + cb * 32, r);
         tmem_wait_ld();
@@ -354,8 +389,9 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       }
       tc_fence_before();
       fence_proxy_async();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (warp == 4 && lane == 0) {
+        mbar_arrive(acc2_empty);  // every thread has read its part of the accumulator
         if (ok) {
 #pragma unroll
           for (int a = 0; a < T::kAtoms; ++a)
@@ -363,7 +399,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           tma_commit_group();
           tma_wait_group_read<0>();
         }
-        mbar_arrive(acc2_empty);  // the accumulator and the tile's shared memory are free
+        mbar_arrive(&x_free[xb]);  // the store has read the buffer
       }
     }
     if (warp == 4 && lane == 0) tma_wait_group<0>();
