@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Per-operator timings of the fused Evoformer ops at the pair / MSA sizes of the configs (one JSON line per op).
 
-  python colabfold-kernels_b200/bench_ops.py [--ops all|name,name] [--rows M] [--n N] [--iters K]
+  python bench_ops.py [--ops all|name,name] [--rows M] [--n N] [--iters K]
 
 HBM-bound ops report GB/s of ALGORITHMIC bytes (every activation read once and written once) and the fraction of
 the measured copy bandwidth; contraction-bound ops report TFLOP/s against the measured dense bf16 peak.  Inputs of
@@ -16,14 +16,14 @@ import sys
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.join(HERE, "colabfold-kernels_b200"))
 from colabfold_kernels import ops  # noqa: E402
 
 bf = torch.bfloat16
 
 
 def peaks():
-  path = os.path.join(HERE, "..", "MEASURED_PEAKS.json")
+  path = os.path.join(HERE, "MEASURED_PEAKS.json")
   if os.path.exists(path):
     d = json.load(open(path))
     return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
@@ -74,6 +74,16 @@ def make_cases(m, n, c=128):
   qscale = torch.tensor([d ** -0.5 * 1.4426950408889634, 1.0], device=dev)
   qk8 = (pk[:, :, :2].float() * qscale[None, None, :, None, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
   vg = pk[:, :, 2:].contiguous()
+  # the block's two transitions: pair [m, 128] with 512 hidden, MSA [m / 2, 256] with 1024 hidden
+  tw1 = (rnd(c, 4 * c) * c ** -0.5).to(bf)
+  tw2 = (rnd(4 * c, c) * (4 * c) ** -0.5).to(bf)
+  tb1, tb2 = torch.zeros(4 * c, device=dev, dtype=bf), torch.zeros(c, device=dev, dtype=bf)
+  c2, m2 = 2 * c, m // 2
+  x2 = rnd(m2, c2).to(bf)
+  ones2, zeros2 = torch.ones(c2, device=dev), torch.zeros(c2, device=dev)
+  uw1 = (rnd(c2, 4 * c2) * c2 ** -0.5).to(bf)
+  uw2 = (rnd(4 * c2, c2) * (4 * c2) ** -0.5).to(bf)
+  ub1, ub2 = torch.zeros(4 * c2, device=dev, dtype=bf), torch.zeros(c2, device=dev, dtype=bf)
   attn_flops = 4.0 * n * h * n * n * d
   attn_bytes = 5 * n * n * h * d * E + h * n * n * E + n * n
   return {
@@ -92,6 +102,10 @@ def make_cases(m, n, c=128):
       "output_projection": (lambda: ops.output_projection(x, w, b, res), 3 * m * c * E, 2.0 * m * c * c),
       "opm_projection": (lambda: ops.opm_projection(x, ones, zeros, lw, lb, lw, lb, mask), m * c * E + 2 * m * 32 * E + m * E,
                          2.0 * m * c * 64),
+      "transition_pair": (lambda: ops.transition(x, ones, zeros, tw1, tb1, tw2, tb2, add_input=True), 2 * m * c * E,
+                          16.0 * m * c * c),
+      "transition_msa": (lambda: ops.transition(x2, ones2, zeros2, uw1, ub1, uw2, ub2, add_input=True), 2 * m2 * c2 * E,
+                         16.0 * m2 * c2 * c2),
       "contract_bf16": (lambda: ops.contract(a, a2), 3 * c * n * n * E, 2.0 * c * n ** 3),
       "contract_e4m3": (lambda: ops.contract(a8, b8), 2 * c * n * n + c * n * n * E, 2.0 * c * n ** 3),
   }
@@ -113,7 +127,7 @@ def main():
     fn, nbytes, flops = cases[name]
     ms = timed(fn, args.iters)
     gbs, tfs = nbytes / ms / 1e6, flops / ms / 1e9
-    tensor_bound = name.startswith("contract") or name.startswith("packed_attention")
+    tensor_bound = name.startswith(("contract", "packed_attention", "transition"))
     print(json.dumps({
         "op": name, "rows": args.rows if not tensor_bound else None, "n": args.n if tensor_bound else None, "ms": round(ms, 4),
         "gb_per_s": round(gbs, 1), "tflop_per_s": round(tfs, 1), "bound": "tensor" if tensor_bound else "hbm",
