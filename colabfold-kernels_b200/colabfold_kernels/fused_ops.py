@@ -138,15 +138,19 @@ def ln_gated_dual_proj(global_config, dtype, num_channel, num_intermediate):
 
 def fp8_contraction(global_config, dtype, num_channel, num_intermediate, num_res):
   """-> (projection, contract) or None: the projection writing e4m3 halves padded to 16 and their contraction
-  (fused_ops.py:262-275)."""
+  (fused_ops.py:262-275).  global_config.fp8_scale (default 1.0) is a per-tensor scale applied before rounding and
+  undone by the contraction."""
   if not global_config.get("fp8", False) or num_res % 8 != 0:
     return None
   if ln_gated_dual_proj(global_config, dtype, num_channel, num_intermediate) is None:
     return None
   from colabfold_kernels import grads, ops, reference
-  proj = grads.differentiable_via(functools.partial(ops.ln_gated_dual_proj, fp8=True, pad=16),
+  # per-tensor scale of the e4m3 operands (global_config.fp8_scale, default 1.0 = the reference's unscaled cast,
+  # tri_mul.py:228): the projection rounds value * scale, the contraction multiplies by 1 / scale^2
+  scale = float(global_config.get("fp8_scale", 1.0))
+  proj = grads.differentiable_via(functools.partial(ops.ln_gated_dual_proj, fp8=True, pad=16, fp8_scale=scale),
                                   functools.partial(reference.ref_ln_gdp, pad=16), nondiff=("eps", "transpose"))
-  return proj, grads.differentiable_via(ops.contract, reference.ref_contract)
+  return proj, grads.differentiable_via(functools.partial(ops.contract, alpha=1.0 / (scale * scale)), reference.ref_contract)
 
 
 def contraction(global_config, dtype):

@@ -222,8 +222,12 @@ def gated_dual_proj(x, wp, bp, wg, bg, mask, split=False, channel_major=False, a
   return (out0, out1) if split else out0
 
 
-def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, transpose=False, pad=1, fp8=False):
-  """-> left, right channel-major: [p/2, m'] for x [m,k], [p/2, a, b'] / [p/2, b, a'] for the pair x [a,b,k]."""
+def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, transpose=False, pad=1, fp8=False,
+                       fp8_scale=1.0):
+  """-> left, right channel-major: [p/2, m'] for x [m,k], [p/2, a, b'] / [p/2, b, a'] for the pair x [a,b,k].
+  fp8 stores e4m3 of value * fp8_scale (per-tensor scale; contract(..., alpha=1 / scale**2) undoes it)."""
+  if not fp8_scale > 0:
+    raise ValueError("ln_gated_dual_proj: fp8_scale must be positive")
   x = _c(x)
   dt = x.dtype
   k, p = x.shape[-1], wp.shape[1]
@@ -240,7 +244,7 @@ def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, t
   with torch.cuda.device(x.device):
     _lib.call("cfk_ln_gated_dual_proj", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(wp.to(dt))),
               _ptr(_c(bp.to(dt))), _ptr(_c(wg.to(dt))), _ptr(_c(bg.to(dt))), _ptr(_c(mask.to(dt))), _ptr(left),
-              _ptr(right), a, b, k, p, int(transpose), int(pad), int(fp8), float(eps), _stream())
+              _ptr(right), a, b, k, p, int(transpose), int(pad), int(fp8), float(fp8_scale), float(eps), _stream())
   return left, right
 
 

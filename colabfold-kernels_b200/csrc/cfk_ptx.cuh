@@ -57,16 +57,8 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Poll limit of every wait.  try_wait itself blocks for a hardware-chosen slice, so 2^22 polls is
-// seconds of wall clock: far beyond any legitimate wait here, short enough to end a broken run.
-constexpr uint32_t kWaitPolls = 1u << 22;
-
-// Returns false when the barrier did not flip within the poll limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
+// Waiting on a barrier is always bounded: mbar_wait_deadline (attention_sm100.cuh) polls try_wait and gives up 2^30
+// clocks after the first failed poll.
 
 // ---------------------------------------------------------------- TMA (cp.async.bulk.tensor), no multicast
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {

@@ -83,9 +83,10 @@ extern "C" int cfk_gated_dual_proj(const void* x, const void* wp, const void* bp
 extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, const float* ln_offset, const void* wp,
                                       const void* bp, const void* wg, const void* bg, const void* mask, void* left,
                                       void* right, int64_t a, int64_t b, int k, int p, int transpose, int pad, int fp8,
-                                      float eps, void* stream) {
+                                      float fp8_scale, float eps, void* stream) {
   if (!x || !ln_scale || !ln_offset || !wp || !bp || !wg || !bg || !mask || !left || !right) return CFK_ERR_NULL;
   if (a <= 0 || b < 0 || p <= 0 || p % 16 != 0 || pad < 1) return CFK_ERR_SHAPE;
+  if (fp8 && !(fp8_scale > 0.f)) return CFK_ERR_SHAPE;
   if (!k_ok(k)) return CFK_ERR_UNSUPPORTED;
   const int ci = p / 2;
   RowGemmParams prm{};
@@ -107,7 +108,7 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   prm.bias[0] = bp; prm.bias[1] = bg; prm.bias_len = p;
   prm.rowmask = mask; prm.rowmask_dtype = CFK_BF16;
   prm.out[0] = left; prm.out[1] = right;
-  prm.ldo = ci; prm.out_dtype = fp8 ? CFK_E4M3 : CFK_BF16; prm.out_scale = 1.f;
+  prm.ldo = ci; prm.out_dtype = fp8 ? CFK_E4M3 : CFK_BF16; prm.out_scale = fp8 ? fp8_scale : 1.f;
   prm.out_channel_major = 1; prm.n_valid = ci;
   // the mask doubles as the row-block filter: a tile of zeros skips the work, a tile below zero is left unwritten
   prm.keep = mask; prm.keep_dtype = CFK_BF16;

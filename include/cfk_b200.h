@@ -189,14 +189,16 @@ CFK_API int cfk_gated_dual_proj(const void* x, const void* wp, const void* bp, c
 /* LayerNorm fused in front of the split channel-major gated dual projection.  b == 0: x [a,k], mask [a] ->
  * left, right [p/2, a'].  b > 0: the pair x [a,b,k], mask [a,b] -> [p/2, a, b'] or, with transpose (the pair read
  * transposed, for incoming edges), [p/2, b, a'].  The primed axis is zero-padded to a multiple of `pad`;
- * negative mask values count as zero; fp8 stores saturating unscaled e4m3.  ln_scale, ln_offset fp32 [k].
+ * negative mask values count as zero; fp8 stores saturating e4m3 of value * fp8_scale (a per-tensor scale chosen by
+ * the caller, > 0; 1.0 is the reference's unscaled cast, tri_mul.py:228; the contraction undoes two scaled operands
+ * with alpha = 1 / (scale_left * scale_right) on cfk_contract).  ln_scale, ln_offset fp32 [k].
  * The mask also filters 128-row tiles: a tile whose mask is all zero gets zeros without its rows being read, a tile
  * whose mask is below zero everywhere is not written (transition.py:29-38).
  * Replaces ln_gated_dual_proj, tri_mul.py:222-283 (FFI: volta.py:328-334). */
 CFK_API int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, const float* ln_offset, const void* wp,
                                    const void* bp, const void* wg, const void* bg, const void* mask, void* left,
                                    void* right, int64_t a, int64_t b, int k, int p, int transpose, int pad, int fp8,
-                                   float eps, void* stream);
+                                   float fp8_scale, float eps, void* stream);
 
 /* Triangle-multiplication output: out = (LN(x_cm^T) wo + bo) * sigmoid(g wg + bg) (+ residual | + act).
  * x_cm [c,m] channel-major product (x_cm_dtype CFK_BF16 or CFK_F32); act [m,ca] is the gate input: already normed

@@ -85,7 +85,7 @@ def test_blocks_below_zero_are_left_unwritten():
   r2 = torch.full_like(r, 7.0)
   from colabfold_kernels import _lib
   _lib.call("cfk_ln_gated_dual_proj", x.data_ptr(), sc.data_ptr(), of.data_ptr(), wp.data_ptr(), bp.data_ptr(), wp.data_ptr(),
-            bp.data_ptr(), mask.data_ptr(), l2.data_ptr(), r2.data_ptr(), m, 0, c, 256, 0, 1, 0, 1e-5,
+            bp.data_ptr(), mask.data_ptr(), l2.data_ptr(), r2.data_ptr(), m, 0, c, 256, 0, 1, 0, 1.0, 1e-5,
             torch.cuda.current_stream().cuda_stream)
   torch.cuda.synchronize()
   assert torch.equal(l2[:, :256], l[:, :256]) and torch.equal(r2[:, :256], r[:, :256])

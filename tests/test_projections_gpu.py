@@ -86,6 +86,37 @@ def test_ln_gdp_pair(transpose, fp8):
   assert float(l.cpu().float()[..., inner:].abs().max()) == 0.0
 
 
+def test_ln_gdp_e4m3_per_tensor_scale():
+  """A projection whose values sit below e4m3's normal range (weights scaled by 2^-7): unscaled, the cast flushes
+  most of them (large error); with a per-tensor scale of 2^7 before rounding and alpha = 2^-14 on the contraction the
+  product meets the e4m3 bound.  Through ops and through the fp8_contraction selector."""
+  from colabfold_kernels import dispatch, fused_ops, ops
+  rng = np.random.default_rng(21)
+  n, k, p = 128, 128, 256
+  x = rnd(rng, n, n, k)
+  wp, bp = rnd(rng, k, p, s=k ** -.5) * 2 ** -7, torch.zeros(p, dtype=bf)
+  wg, bg = rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1)
+  sc, of = 1 + rnd(rng, k, s=.1).float(), rnd(rng, k, s=.1).float()
+  mask = torch.ones(n, n, dtype=bf)
+  rl, rr = O.ref_ln_gdp(x, sc, of, wp, bp, wg, bg, mask, pad=16)
+  ref = O.ref_contract(rl, rr)
+  dev = [t.cuda() for t in (x, sc, of, wp, bp, wg, bg, mask)]
+  errs = {}
+  for scale in (1.0, 128.0):
+    l, r = ops.ln_gated_dual_proj(*dev, pad=16, fp8=True, fp8_scale=scale)
+    assert l.dtype == torch.float8_e4m3fn
+    errs[scale] = O.rel_err(ops.contract(l, r, alpha=1.0 / scale ** 2).cpu().float(), ref)
+  assert errs[128.0] <= 6e-2 < errs[1.0], errs
+  sel = fused_ops.fp8_contraction({**dispatch(), "fp8": True, "fp8_scale": 128.0}, bf, k, p // 2, n)
+  assert sel is not None
+  proj, contract = sel
+  l, r = proj(*dev, eps=1e-5)
+  assert O.rel_err(contract(l, r).cpu().float(), ref) <= 6e-2
+  with pytest.raises(ValueError):
+    ops.ln_gated_dual_proj(*dev, pad=16, fp8=True, fp8_scale=0.0)
+  assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("m,c,xdt", [(4096, 128, bf), (999, 128, bf), (500, 64, bf), (1, 128, bf), (127, 128, bf),
                                      (999, 128, torch.float32)])
 def test_trimul_epilogue(m, c, xdt):
