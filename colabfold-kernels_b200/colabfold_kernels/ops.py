@@ -428,6 +428,52 @@ def opm_update(lhs, t, bias, norm, residual=None, eps=1e-3):
   return opm_finish(x, bias, norm, None if residual is None else residual.to(dt), eps)
 
 
+def opm_projection_cm(x, ln_scale, ln_offset, lw, lb, rw, rb, mask, eps=1e-5):
+  """opm_projection for the fused outer product mean: x [s, r, c], mask [s, r] -> left, right [k, r, pitch], channel-major
+  with the MSA depth contiguous (pitch = s rounded up to 8, the tail zeros)."""
+  x = _c(x)
+  dt = x.dtype
+  s, r, c = x.shape
+  k = lw.shape[1]
+  pitch = -(-s // 8) * 8
+  left = torch.empty((k, r, pitch), dtype=dt, device=x.device)
+  right = torch.empty((k, r, pitch), dtype=dt, device=x.device)
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_opm_projection_cm", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(lw.to(dt))),
+              _ptr(_c(lb.to(dt))), _ptr(_c(rw.to(dt))), _ptr(_c(rb.to(dt))), _ptr(_c(mask.to(dt))), _ptr(left), _ptr(right),
+              s, r, c, k, pitch, float(eps), _stream())
+  return left, right
+
+
+def opm_fused_supported(c, f, dtype):
+  """What cfk_opm_fused takes: 32-channel bf16 projections and 128 output channels."""
+  return c == 32 and f == 128 and dtype == torch.bfloat16
+
+
+def outer_product_mean_cm(left_cm, right_cm, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+  """Deep-MSA outer product mean in one kernel from the channel-major projections of opm_projection_cm: left_cm
+  [c, ri, pitch], right_cm [c, rj, pitch], masks [s, ri] / [s, rj], w [c*c, f] -> [ri, rj, f].  The outer product stays on
+  chip (rounded to bf16 before the output weights, as the reference's opm_outer rounds it, opm.py:124-134); the mask
+  overlap count comes from a kernel of the library (cfk_opm_norm)."""
+  left_cm, right_cm = _c(left_cm), _c(right_cm)
+  dt = left_cm.dtype
+  c, ri, pitch = left_cm.shape
+  rj, f = right_cm.shape[1], w.shape[1]
+  depth = mask_left.shape[0]
+  if right_cm.shape[0] != c or right_cm.shape[2] != pitch or w.shape[0] != c * c or mask_right.shape[0] != depth:
+    raise ValueError("outer_product_mean_cm: operand shapes disagree")
+  ml = _c(mask_left if mask_left.dtype in (torch.float32, torch.bfloat16) else mask_left.float())
+  mr = _c(mask_right.to(ml.dtype))
+  norm = torch.empty((ri, rj), dtype=torch.float32, device=left_cm.device)
+  out = torch.empty((ri, rj, f), dtype=dt, device=left_cm.device)
+  res = None if residual is None else _c(residual.to(dt))
+  with torch.cuda.device(left_cm.device):
+    _lib.call("cfk_opm_norm", _ptr(ml), _ptr(mr), tag(ml.dtype), _ptr(norm), depth, ri, rj, _stream())
+    _lib.call("cfk_opm_fused", _ptr(left_cm), _ptr(right_cm), _ptr(_c(w.to(dt))), _ptr(_c(bias.to(dt))), _ptr(norm), _ptr(res),
+              _ptr(out), ri, rj, depth, pitch, c, f, float(eps), _stream())
+  return out
+
+
 def outer_product_mean(left, right, mask_left, mask_right, w, bias, residual=None, eps=1e-3, fp8=False):
   """Deep-MSA outer product mean from the masked projections left [s, ri, c], right [s, rj, c]: two tensor-core GEMMs
   (the outer product over the MSA depth, rounded to bf16 as the reference's opm_outer does, opm.py:124-134; then the

@@ -256,6 +256,32 @@ CFK_API int cfk_opm_projection(const void* x, const float* ln_scale, const float
                                const void* lb, const void* rw, const void* rb, const void* mask, void* left,
                                void* right, int64_t m, int c, int k, float eps, void* stream);
 
+/* The same two projections written channel-major with the MSA depth contiguous: x [s,r,c], mask [s,r] ->
+ * left, right [k, r, pitch] (pitch >= s, a multiple of 8; columns s..pitch-1 are zeros); k <= 64.  This is the operand
+ * layout of cfk_opm_fused.  The reference's opm_projection (opm.py:36-59) writes [s,r,k]; the layout is internal to
+ * the deep outer product mean. */
+CFK_API int cfk_opm_projection_cm(const void* x, const float* ln_scale, const float* ln_offset, const void* lw,
+                                  const void* lb, const void* rw, const void* rb, const void* mask, void* left,
+                                  void* right, int64_t s, int64_t r, int c, int k, int64_t pitch, float eps,
+                                  void* stream);
+
+/* norm[i,j] = sum_s mask_left[s,i] * mask_right[s,j] in fp32: the overlap count the outer product mean divides by
+ * (ColabFold computes it with an XLA einsum; no kernel of the reference).  Masks [depth, ri], [depth, rj] in
+ * mask_dtype (CFK_BF16 or CFK_F32). */
+CFK_API int cfk_opm_norm(const void* mask_left, const void* mask_right, int mask_dtype, float* norm, int depth, int ri,
+                         int rj, void* stream);
+
+/* Deep outer product mean in one kernel:
+ * out[i,j,:] = ((sum_s left[:,i,s] (x) right[:,j,s]) rounded to bf16 . w + bias) / (eps + norm[i,j]) (+ residual[i,j,:]).
+ * left_cm [c, ri, pitch], right_cm [c, rj, pitch] bf16 (cfk_opm_projection_cm), w [c*c, f] bf16 with row index
+ * a*c + b, bias [f] bf16, norm [ri,rj] fp32, residual (or NULL) and out [ri,rj,f] bf16 (out may alias residual).
+ * c == 32 and f == 128, else CFK_ERR_UNSUPPORTED (the caller composes cfk_opm_outer_product, cfk_contract and
+ * cfk_opm_finish).  The outer product never reaches memory, as in the reference's opm_outer (opm.py:122-162: per left
+ * channel the product is rounded to the input type, then multiplied by its rows of w), here at any MSA depth. */
+CFK_API int cfk_opm_fused(const void* left_cm, const void* right_cm, const void* w, const void* bias, const float* norm,
+                          const void* residual, void* out, int ri, int rj, int depth, int64_t pitch, int c, int f,
+                          float eps, void* stream);
+
 /* Outer-product-mean tail: out[m,f] = (x[m,f] + bias[f]) / (eps + norm[m]) + residual[m,f] (residual may be NULL,
  * out may alias it); x, bias, residual, out bf16, norm fp32.  The pair update of opm_update, opm.py:69-88,116-119,
  * applied after the two GEMMs of the deep-MSA outer product (cfk_contract). */

@@ -181,3 +181,47 @@ def test_contract_exchanged_reads_and_writes_the_all_to_all_layouts(split_k, dty
   assert ops.device_status() == 0
   want = torch.stack(whole.chunk(parts, dim=1), 0)
   assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("s,ri,rj,cm", [(70, 40, 40, 256), (64, 16, 8, 128), (200, 37, 53, 256), (512, 128, 256, 256)])
+def test_fused_outer_product_mean(s, ri, rj, cm):
+  """The one-kernel deep outer product mean (channel-major projections with the depth contiguous, outer product kept on
+  chip, mask overlap count from the library) against the oracle, and against the three-kernel composition it
+  replaces; ragged depth (70: pitch 72, tail beyond the last 64-deep slice), residue counts off the 16 x 8 tile,
+  ri != rj (a row shard of the pair)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(s + ri)
+  mk = lambda *sh, sc=1.0: torch.from_numpy((rng.standard_normal(sh) * sc).astype(np.float32)).to(torch.bfloat16)
+  r = max(ri, rj)
+  m = mk(s, r, cm)
+  gamma, beta = 1 + mk(cm, sc=.02).float(), mk(cm, sc=.02).float()
+  lw, rw = mk(cm, 32, sc=cm ** -.5), mk(cm, 32, sc=cm ** -.5)
+  lb, rb = mk(32, sc=.1), mk(32, sc=.1)
+  w, bias, res = mk(32 * 32, 128, sc=1 / 32), mk(128, sc=.1), mk(ri, rj, 128)
+  mask = torch.from_numpy((rng.random((s, r)) < .9).astype(np.float32)).to(torch.bfloat16)
+  cu = lambda *t: [x.cuda() for x in t]
+  lcm, rcm = ops.opm_projection_cm(*cu(m, gamma, beta, lw, lb, rw, rb, mask))
+  assert lcm.shape == (32, r, -(-s // 8) * 8)
+  rl, rr = O.ref_opm_projection(m.reshape(s * r, cm), gamma, beta, lw, lb, rw, rb, mask.reshape(-1))
+  rl, rr = rl.reshape(s, r, 32), rr.reshape(s, r, 32)
+  # the projections themselves, in their new layout (and an exactly zero tail)
+  assert O.rel_err(lcm[:, :, :s].permute(2, 1, 0).cpu().float(), rl) <= 2e-2
+  assert O.rel_err(rcm[:, :, :s].permute(2, 1, 0).cpu().float(), rr) <= 2e-2
+  assert float(lcm[:, :, s:].float().abs().max() if lcm.shape[2] > s else 0.0) == 0.0
+  lcm, rcm = lcm[:, :ri].contiguous(), rcm[:, :rj].contiguous()
+  got = ops.outer_product_mean_cm(lcm, rcm, mask[:, :ri].cuda(), mask[:, :rj].cuda(), w.cuda(), bias.cuda(), residual=res.cuda())
+  assert ops.device_status() == 0
+  # oracle on the projections the kernel saw (bf16), so the bound is the GEMMs' alone
+  lq, rq = lcm[:, :, :s].permute(2, 1, 0).cpu().float(), rcm[:, :, :s].permute(2, 1, 0).cpu().float()
+  outer = torch.einsum("sia,sjb->ijab", lq, rq).reshape(ri, rj, 1024)
+  ref = (outer @ w.float() + bias.float()) / (1e-3 + mask[:, :ri].float().T @ mask[:, :rj].float())[..., None] + res.float()
+  assert O.rel_err(got.cpu().float(), ref) <= 2e-2
+  # and the composition of the three kernels on the same projections (it needs a depth in whole 16-byte rows)
+  if s % 8 == 0:
+    comp = ops.outer_product_mean(lcm[:, :, :s].permute(2, 1, 0).contiguous(), rcm[:, :, :s].permute(2, 1, 0).contiguous(),
+                                  mask[:, :ri].cuda(), mask[:, :rj].cuda(), w.cuda(), bias.cuda(), residual=res.cuda())
+    assert O.rel_err(got.cpu().float(), comp.cpu().float()) <= 1e-2
+  # without a residual, and the unsupported widths say so
+  got0 = ops.outer_product_mean_cm(lcm, rcm, mask[:, :ri].cuda(), mask[:, :rj].cuda(), w.cuda(), bias.cuda())
+  assert O.rel_err(got0.cpu().float(), ref - res.float()) <= 2e-2
+  assert not ops.opm_fused_supported(16, 128, torch.bfloat16) and ops.opm_fused_supported(32, 128, torch.bfloat16)
