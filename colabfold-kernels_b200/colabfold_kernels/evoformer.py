@@ -61,8 +61,7 @@ def init_params(c_m=256, c_z=128, heads_msa=8, heads_pair=4, d_head=32, c_opm=32
 
 
 def cuda_kernels():
-  """The production namespace: every op is a kernel of libcfk_b200 except the second GEMM of the two transitions,
-  which is the library GEMM (LayerNorm, the first GEMM, its bias and the relu are one kernel of the library)."""
+  """The production namespace: every op is a kernel of libcfk_b200."""
   from colabfold_kernels import ops
 
   def transition(x, ln, w1, b1, w2, b2):
@@ -71,6 +70,7 @@ def cuda_kernels():
   return types.SimpleNamespace(
       ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,
       opm_projection=ops.opm_projection, outer_product_mean=ops.outer_product_mean,
+      opm_projection_cm=ops.opm_projection_cm, outer_product_mean_cm=ops.outer_product_mean_cm,
       ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, contract_gathered=ops.contract_gathered,
       contract_exchanged=ops.contract_exchanged,
       trimul_epilogue=ops.trimul_epilogue,
@@ -128,8 +128,12 @@ def block(K, msa, pair, msa_mask, pair_mask, params, fp8_trimul=False, fp8_atten
   msa = attend(K, msa, params["col_attn"], None, mm.t().contiguous(), True, d, **fa)
   msa = transition(K, msa, params["msa_transition"])
   o = params["opm"]
-  left, right = K.opm_projection(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
-  pair = K.outer_product_mean(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair, **({"fp8": True} if fp8_opm else {}))
+  if fp8_opm:  # the e4m3 outer product keeps the three-kernel form
+    left, right = K.opm_projection(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
+    pair = K.outer_product_mean(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair, fp8=True)
+  else:  # projections channel-major with the depth contiguous, then one kernel with the outer product on chip
+    left, right = K.opm_projection_cm(msa, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], msa_mask.to(msa.dtype))
+    pair = K.outer_product_mean_cm(left, right, msa_mask, msa_mask, o["w"], o["b"], residual=pair)
   for name, incoming in (("tri_out", False), ("tri_in", True)):
     t = params[name]
     l, r = K.ln_gated_dual_proj(pair, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], pair_mask.to(pair.dtype),
@@ -297,8 +301,12 @@ class ShardedBlock:
     # 4 outer product mean: local left projection against everyone's right projection -> local pair rows
     o = prm["opm"]
     mloc = msa_mask[:, rs].contiguous()
-    left, right = K.opm_projection(msa_c, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], mloc.to(msa_c.dtype))
-    pair_r = K.outer_product_mean(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r, **self.fo)
+    if self.fo:
+      left, right = K.opm_projection(msa_c, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], mloc.to(msa_c.dtype))
+      pair_r = K.outer_product_mean(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r, **self.fo)
+    else:
+      left, right = K.opm_projection_cm(msa_c, o["ln"][0], o["ln"][1], o["lw"], o["lb"], o["rw"], o["rb"], mloc.to(msa_c.dtype))
+      pair_r = K.outer_product_mean_cm(left, self.gather(right, 1), mloc, msa_mask, o["w"], o["b"], residual=pair_r)
     msa_s = self.cols_to_rows(msa_c)
     # 5 triangle multiplication, outgoing edges: local rows of the left operand, all rows of the right
     t = prm["tri_out"]

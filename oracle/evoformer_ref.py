@@ -27,6 +27,15 @@ def oracle_kernels(dtype=torch.float32):
     out = out / (eps + mask_left.to(dtype).T @ mask_right.to(dtype))[..., None]
     return out if residual is None else out + residual.to(dtype)
 
+  def opm_projection_cm(x, s, o, lw, lb, rw, rb, mask, eps=1e-5):
+    # x [depth, r, c] -> left, right [k, r, depth]: the projections channel-major with the MSA depth contiguous
+    depth, r, c = x.shape
+    left, right = R.ref_opm_projection(x.reshape(depth * r, c), s, o, lw, lb, rw, rb, mask.reshape(-1), eps=eps, dtype=dtype)
+    return tuple(t.reshape(depth, r, -1).permute(2, 1, 0).contiguous() for t in (left, right))
+
+  def outer_product_mean_cm(left_cm, right_cm, mask_left, mask_right, w, bias, residual=None, eps=1e-3):
+    return outer_product_mean(left_cm.permute(2, 1, 0), right_cm.permute(2, 1, 0), mask_left, mask_right, w, bias, residual, eps)
+
   def ln_gated_dual_proj(x, s, o, wp, bp, wg, bg, mask, eps=1e-5, transpose=False, pad=1):
     return R.ref_ln_gdp(x, s, o, wp, bp, wg, bg, mask, eps=eps, transpose=transpose, pad=pad, dtype=dtype)
 
@@ -55,6 +64,7 @@ def oracle_kernels(dtype=torch.float32):
 
   return types.SimpleNamespace(ln_projection=ln_projection, packed_attention=packed_attention,
                                output_projection=output_projection, opm_projection=opm_projection,
-                               outer_product_mean=outer_product_mean, ln_gated_dual_proj=ln_gated_dual_proj,
+                               outer_product_mean=outer_product_mean, opm_projection_cm=opm_projection_cm,
+                               outer_product_mean_cm=outer_product_mean_cm, ln_gated_dual_proj=ln_gated_dual_proj,
                                contract=contract, contract_gathered=contract_gathered, contract_exchanged=contract_exchanged,
                                trimul_epilogue=trimul_epilogue, transition=transition)
