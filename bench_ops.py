@@ -84,6 +84,17 @@ def make_cases(m, n, c=128):
   uw1 = (rnd(c2, 4 * c2) * c2 ** -0.5).to(bf)
   uw2 = (rnd(4 * c2, c2) * (4 * c2) ** -0.5).to(bf)
   ub1, ub2 = torch.zeros(4 * c2, device=dev, dtype=bf), torch.zeros(c2, device=dev, dtype=bf)
+  # outer product mean at N_seq 512: projections of the MSA [512, n, 256] and the fused product / mean / output linear
+  depth, cm = 512, 256
+  msa = rnd(depth, n, cm).to(bf)
+  ones_m, zeros_m = torch.ones(cm, device=dev), torch.zeros(cm, device=dev)
+  ow = (rnd(cm, 32) * cm ** -0.5).to(bf)
+  ob = torch.zeros(32, device=dev, dtype=bf)
+  omask = (torch.rand(depth, n, device=dev, generator=g) < 0.95).to(bf)
+  opm_w = (rnd(1024, c) / 32).to(bf)
+  pair_res = rnd(n, n, c).to(bf)
+  lcm, rcm = ops.opm_projection_cm(msa, ones_m, zeros_m, ow, ob, ow, ob, omask)
+  opm_flops = 2.0 * n * n * 1024 * (depth + c)
   attn_flops = 4.0 * n * h * n * n * d
   attn_bytes = 5 * n * n * h * d * E + h * n * n * E + n * n
   return {
@@ -106,6 +117,10 @@ def make_cases(m, n, c=128):
                           16.0 * m * c * c),
       "transition_msa": (lambda: ops.transition(x2, ones2, zeros2, uw1, ub1, uw2, ub2, add_input=True), 2 * m2 * c2 * E,
                          16.0 * m2 * c2 * c2),
+      "opm_projection_cm": (lambda: ops.opm_projection_cm(msa, ones_m, zeros_m, ow, ob, ow, ob, omask),
+                            depth * n * cm * E + 2 * depth * n * 32 * E + depth * n * E, 2.0 * depth * n * cm * 64),
+      "outer_product_mean_fused": (lambda: ops.outer_product_mean_cm(lcm, rcm, omask, omask, opm_w, b, residual=pair_res),
+                                   2 * depth * n * 32 * E + 2 * n * n * c * E, opm_flops),
       "contract_bf16": (lambda: ops.contract(a, a2), 3 * c * n * n * E, 2.0 * c * n ** 3),
       "contract_e4m3": (lambda: ops.contract(a8, b8), 2 * c * n * n + c * n * n * E, 2.0 * c * n ** 3),
   }
@@ -127,7 +142,7 @@ def main():
     fn, nbytes, flops = cases[name]
     ms = timed(fn, args.iters)
     gbs, tfs = nbytes / ms / 1e6, flops / ms / 1e9
-    tensor_bound = name.startswith(("contract", "packed_attention", "transition"))
+    tensor_bound = name.startswith(("contract", "packed_attention", "transition", "outer_product_mean"))
     print(json.dumps({
         "op": name, "rows": args.rows if not tensor_bound else None, "n": args.n if tensor_bound else None, "ms": round(ms, 4),
         "gb_per_s": round(gbs, 1), "tflop_per_s": round(tfs, 1), "bound": "tensor" if tensor_bound else "hbm",

@@ -410,8 +410,24 @@ def _outer_product(left, right, fp8=False):
 def opm_outer(left, right, w):
   """The outer product mean in AF2's own order (opm.py:147-168): left [rows, B, C], right [rows, D, E], w [C*E, F] ->
   [B, D, F] in left's dtype; the rows' outer product rounded to left's dtype, then w over (c, e)."""
-  _, bdim, c = left.shape
+  rows, bdim, c = left.shape
   ddim, e = right.shape[1], right.shape[2]
+  if e == c and opm_fused_supported(c, w.shape[1], left.dtype) and right.dtype == left.dtype:
+    # one kernel, the product never written (as the reference's kernel): the operands channel-major with the rows
+    # contiguous (a copy of rows * (B + D) * C values), a unit normaliser and no bias turn the deep form into this one
+    pitch = -(-rows // 8) * 8
+    lcm = torch.zeros((c, bdim, pitch), dtype=left.dtype, device=left.device)
+    rcm = torch.zeros((e, ddim, pitch), dtype=left.dtype, device=left.device)
+    lcm[:, :, :rows] = left.permute(2, 1, 0)
+    rcm[:, :, :rows] = right.permute(2, 1, 0)
+    f = w.shape[1]
+    out = torch.empty((bdim, ddim, f), dtype=left.dtype, device=left.device)
+    norm = torch.ones((bdim, ddim), dtype=torch.float32, device=left.device)
+    zero = torch.zeros(f, dtype=left.dtype, device=left.device)
+    with torch.cuda.device(left.device):
+      _lib.call("cfk_opm_fused", _ptr(lcm), _ptr(rcm), _ptr(_c(w.to(left.dtype))), _ptr(zero), _ptr(norm), None, _ptr(out),
+                bdim, ddim, rows, pitch, c, f, 0.0, _stream())
+    return out
   outer = _outer_product(left, right)
   wt = w.to(left.dtype).t().contiguous().view(1, w.shape[1], c * e)
   return contract(outer, wt).view(bdim, ddim, w.shape[1])

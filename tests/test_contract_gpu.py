@@ -225,3 +225,21 @@ def test_fused_outer_product_mean(s, ri, rj, cm):
   got0 = ops.outer_product_mean_cm(lcm, rcm, mask[:, :ri].cuda(), mask[:, :rj].cuda(), w.cuda(), bias.cuda())
   assert O.rel_err(got0.cpu().float(), ref - res.float()) <= 2e-2
   assert not ops.opm_fused_supported(16, 128, torch.bfloat16) and ops.opm_fused_supported(32, 128, torch.bfloat16)
+
+
+def test_opm_outer_selector_takes_the_fused_kernel_and_the_composed_path():
+  """opm_outer at AF2's widths (32 x 32 channels, 128 outputs) runs the one-kernel form (product never written); other
+  widths compose the contraction kernels.  Both against the oracle on the same inputs, through the selector."""
+  from colabfold_kernels import dispatch, fused_ops, ops
+  rng = np.random.default_rng(31)
+  mk = lambda *sh, sc=1.0: torch.from_numpy((rng.standard_normal(sh) * sc).astype(np.float32)).to(torch.bfloat16)
+  for c, f, bdim, ddim in ((32, 128, 40, 24), (16, 64, 40, 24)):
+    left, right, w = mk(16, bdim, c, sc=.5), mk(16, ddim, c, sc=.5), mk(c * c, f, sc=1 / c)
+    sel = fused_ops.opm_outer(dispatch(), torch.bfloat16, 16, c, ddim, f)
+    assert callable(sel)
+    launches = ops._lib.load().cfk_launch_count(1)
+    got = sel(left.cuda(), right.cuda(), w.cuda())
+    launches = ops._lib.load().cfk_launch_count(0)
+    assert launches == (1 if c == 32 else 2), launches      # one kernel of the library, or outer product + output weights
+    assert O.rel_err(got.cpu().float(), O.ref_opm_outer(left, right, w)) <= 2e-2
+  assert ops.device_status() == 0
