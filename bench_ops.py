@@ -57,6 +57,7 @@ def make_cases(m, n, c=128):
   wp = (rnd(c, 2 * c) * c ** -0.5).to(bf)
   bp = torch.zeros(2 * c, device=dev, dtype=bf)
   w4 = (rnd(4, c, c) * c ** -0.5).to(bf)
+  wbias = (rnd(c, 8) * c ** -0.5).to(bf)
   mask = (torch.rand(m, device=dev, generator=g) < 0.95).to(bf)
   res = rnd(m, c).to(bf)
   lw = (rnd(c, 32) * c ** -0.5).to(bf)
@@ -110,6 +111,7 @@ def make_cases(m, n, c=128):
       "trimul_epilogue": (lambda: ops.trimul_epilogue(x_cm, x, ones, zeros, w, b, w, b, in_scale=ones, in_offset=zeros, add_input=True),
                           3 * m * c * E, 4.0 * m * c * c),
       "ln_projection": (lambda: ops.ln_projection(x, ones, zeros, w4, None), m * c * E + 4 * m * c * E, 2.0 * m * c * 4 * c),
+      "ln_head_bias": (lambda: ops.ln_projection(x, ones, zeros, None, wbias), m * c * E + 8 * m * E, 2.0 * m * c * 8),
       "output_projection": (lambda: ops.output_projection(x, w, b, res), 3 * m * c * E, 2.0 * m * c * c),
       "opm_projection": (lambda: ops.opm_projection(x, ones, zeros, lw, lb, lw, lb, mask), m * c * E + 2 * m * 32 * E + m * E,
                          2.0 * m * c * 64),

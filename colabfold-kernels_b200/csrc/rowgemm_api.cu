@@ -184,23 +184,6 @@ extern "C" int cfk_transition_hidden(const void* x, const float* ln_scale, const
   return run_chunks(prm, cps, w1, nullptr, 1, hdim, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const float* ln_offset, const void* wb,
-                                const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
-                                float eps, void* stream) {
-  if (!x || !ln_scale || !ln_offset || !wb || !bias_out) return CFK_ERR_NULL;
-  if (m < 0 || h <= 0 || h > h_padded || h_padded % 8 != 0 || h_padded > 64) return CFK_ERR_SHAPE;
-  if (!k_ok(a)) return CFK_ERR_UNSUPPORTED;
-  if (m == 0) return CFK_OK;
-  RowGemmParams prm{};
-  prm.src[0] = row_major(x, a, ln_scale, ln_offset);
-  prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.eps = eps;
-  prm.mode = kModeLinear; prm.dual = 0; prm.n_chunk = 64;
-  prm.chunks_per_slot = 1; prm.chunks_per_array = 1;
-  prm.out[0] = bias_out; prm.out_channel_major = 1; prm.n_valid = h; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
-  prm.keep = keep; prm.keep_dtype = keep_dtype;
-  return run_chunks(prm, 1, wb, nullptr, 1, h_padded, static_cast<cudaStream_t>(stream));
-}
-
 extern "C" int cfk_output_projection(const void* o, const void* w, const void* b, const void* residual, const void* keep,
                                      int keep_dtype, void* out, int64_t m, int k, int c, void* stream) {
   if (!o || !w || !b || !out) return CFK_ERR_NULL;
