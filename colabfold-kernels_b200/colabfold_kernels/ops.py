@@ -332,27 +332,27 @@ def transition(x, ln_scale, ln_offset, w1, b1, w2, b2, keep=None, eps=1e-5, add_
   library, both GEMMs on the tensor cores and the hidden activation on chip (cfk_transition).  c = 64: LayerNorm, the
   first GEMM, its bias and the relu are one kernel writing the hidden activation in bf16 and the second GEMM is the
   library GEMM.  keep: 128-row blocks it marks nowhere come out as zeros (x with add_input), as the reference leaves
-  them."""
+  them; at c = 128 / 256 the kernel itself skips them."""
   shape = x.shape
   c, hdim = shape[-1], w1.shape[1]
   x2 = _c(x.reshape(-1, c))
   dt = x2.dtype
   m = x2.shape[0]
+  kp, kt = _keep(None if keep is None else keep.reshape(-1))
   if c in (128, 256) and dt == torch.bfloat16:
-    out = torch.empty_like(x2)
+    out = torch.empty_like(x2)  # blocks whose keep is negative throughout stay unwritten, as in the reference
     with torch.cuda.device(x2.device):
       _lib.call("cfk_transition", _ptr(x2), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w1.to(dt))),
-                _ptr(_c(b1.to(dt))), _ptr(_c(w2.to(dt))), _ptr(_c(b2.to(dt))), _ptr(out), m, c, hdim, float(eps),
-                int(add_input), _stream())
-  else:
-    kp, kt = _keep(None if keep is None else keep.reshape(-1))
-    h = torch.empty((m, hdim), dtype=dt, device=x2.device)
-    with torch.cuda.device(x2.device):
-      _lib.call("cfk_transition_hidden", _ptr(x2), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w1.to(dt))),
-                _ptr(_c(b1.to(dt))), _ptr(kp), kt, _ptr(h), m, c, hdim, float(eps), _stream())
-    out = torch.addmm(b2.to(dt), h, w2.to(dt))
-    if add_input:
-      out.add_(x2)
+                _ptr(_c(b1.to(dt))), _ptr(_c(w2.to(dt))), _ptr(_c(b2.to(dt))), _ptr(kp), kt, _ptr(out), m, c, hdim,
+                float(eps), int(add_input), _stream())
+    return out.reshape(shape)
+  h = torch.empty((m, hdim), dtype=dt, device=x2.device)
+  with torch.cuda.device(x2.device):
+    _lib.call("cfk_transition_hidden", _ptr(x2), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w1.to(dt))),
+              _ptr(_c(b1.to(dt))), _ptr(kp), kt, _ptr(h), m, c, hdim, float(eps), _stream())
+  out = torch.addmm(b2.to(dt), h, w2.to(dt))
+  if add_input:
+    out.add_(x2)
   if keep is not None:
     pad = (-m) % 128
     rows = torch.nn.functional.pad(keep.reshape(-1) > 0, (0, pad)).view(-1, 128).any(1).repeat_interleave(128)[:m]

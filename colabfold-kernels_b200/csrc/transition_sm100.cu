@@ -19,6 +19,7 @@ namespace {
 
 constexpr int kRowsT = 128;   // rows per tile = TMEM lanes
 constexpr int kHC = 64;       // hidden columns per chunk
+constexpr int kMaxTilesT = 768;   // tiles per CTA when row blocks may be skipped
 constexpr int kThreadsT = 384;   // warps 0-3 control, 4-7 and 8-11 two worker groups
 
 template <int C>
@@ -38,7 +39,8 @@ struct TrCfg {
   static constexpr int kOffBar = kOffH + kHBufs * kH;
   static constexpr int kNumBars = 6 + 4 * kWRing + 4 + 4 + 2 + 2;
   static constexpr int kOffTmem = kOffBar + kNumBars * 8;
-  static constexpr int kSmem = kOffTmem + 16 + 1024;
+  static constexpr int kOffCls = kOffTmem + 16;           // int8 [kMaxTilesT]: class of each tile this CTA visits
+  static constexpr int kSmem = kOffCls + kMaxTilesT + 1024;
   static constexpr int kColAcc2 = 128;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kOffW1 % 1024 == 0 && kOffW2 % 1024 == 0 && kOffH % 1024 == 0, "swizzled tiles start on their atom");
@@ -55,6 +57,8 @@ struct TrParams {
   int hdim;
   float eps;
   int add_input;
+  const void* keep;            // [M] rows that matter (or null): 128-row blocks it marks nowhere are not computed
+  int keep_dtype;
   int* status;
 };
 
@@ -127,10 +131,39 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  // Row-block skipping (transition.py:29-38): the class of every tile this CTA will visit - 1 compute, 0 no row kept
+  // (the result is x, or zeros without the residual), -1 keep negative throughout (left unwritten) - worked out once
+  // by all warps so that every role takes the same decision.
+  const int8_t* cls = nullptr;
+  if (prm.keep != nullptr) {
+    int8_t* w = reinterpret_cast<int8_t*>(smem + T::kOffCls);
+    for (int i = warp;; i += kThreadsT / 32) {
+      const int64_t tile = blockIdx.x + int64_t(i) * gridDim.x;
+      if (tile >= ntiles) break;
+      float top = -1.f;
+      for (int j = lane; j < kRowsT; j += 32) {
+        const int64_t r = tile * kRowsT + j;
+        if (r < prm.m)
+          top = fmaxf(top, prm.keep_dtype == CFK_F32 ? static_cast<const float*>(prm.keep)[r]
+                                                     : __bfloat162float(static_cast<const __nv_bfloat16*>(prm.keep)[r]));
+      }
+      for (int off = 16; off > 0; off >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+      if (lane == 0) w[i] = top > 0.f ? 1 : (top == 0.f ? 0 : -1);
+    }
+    cls = w;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the next tile this CTA computes at or after its local index seq (-1: none); seq is left on it
+  auto next_computed = [&](uint32_t& seq) -> int64_t {
+    for (;; ++seq) {
+      const int64_t tile = blockIdx.x + int64_t(seq) * gridDim.x;
+      if (tile >= ntiles) return -1;
+      if (cls == nullptr || cls[seq] == 1) return tile;
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -148,10 +181,13 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           tma_load_2d(smem + T::kOffX + xb * T::kTileX + a * (kRowsT * 128), &tm_x, &x_full[xb], a * 64, int(tile * kRowsT));
         return true;
       };
-      if (int64_t(blockIdx.x) < ntiles) ok = load_x(0, blockIdx.x);
-      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++ti) {
+      uint32_t seq = 0;
+      int64_t tile = next_computed(seq);
+      if (tile >= 0) ok = load_x(0, tile);
+      for (; tile >= 0 && ok; ++ti) {
         const int xb = ti % XB;
-        const int64_t next = tile + gridDim.x;
+        uint32_t seq_next = seq + 1;
+        const int64_t next = next_computed(seq_next);
         for (int n = 0; n < nchunks && ok; ++n, ++cc) {
           const int slot = cc % WR;
           const uint32_t par = ((cc / WR) & 1) ^ 1;
@@ -166,7 +202,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           for (int a = 0; a < T::kAtoms; ++a)
             tma_load_2d(smem + T::kOffW2 + slot * T::kW2 + a * (64 * 128), &tm_w2, &w2_full[slot], a * 64, n * kHC);
           // with two buffers the next tile's rows land under this tile's GEMMs
-          if (XB == 2 && n == nchunks / 2 && next < ntiles) ok = load_x(ti + 1, next);
+          if (XB == 2 && n == nchunks / 2 && next >= 0) ok = load_x(ti + 1, next);
         }
         if (ok && prm.add_input) {
           // the raw rows again, over the normalised tile, for the residual: from L2, under the tile's last GEMMs
@@ -177,7 +213,9 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           for (int a = 0; a < T::kAtoms; ++a)
             tma_load_2d(smem + T::kOffX + xb * T::kTileX + a * (kRowsT * 128), &tm_x, xraw_full, a * 64, int(tile * kRowsT));
         }
-        if (XB == 1 && ok && next < ntiles) ok = load_x(ti + 1, next);
+        if (XB == 1 && ok && next >= 0) ok = load_x(ti + 1, next);
+        tile = next;
+        seq = seq_next;
       }
     }
     __syncwarp();
@@ -226,7 +264,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         ++c2;
         return true;
       };
-      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++ti) {
+      uint32_t seq = 0;
+      for (int64_t tile = next_computed(seq); tile >= 0 && ok; tile = next_computed(++seq), ++ti) {
         if (warp == 1) {
           const int xb = ti % XB;
           ok = mbar_wait_deadline(&x_ready[xb], (ti / XB) & 1);
@@ -263,8 +302,25 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     report_timeout(prm.status, (code));                           \
     ok = false;                                                   \
   }
-    uint32_t ti = 0, ce = 0;
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++ti) {
+    uint32_t ti = 0, ce = 0, seq = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++seq) {
+      if (cls != nullptr && cls[seq] != 1) {
+        // not computed: the result is the input (or zeros), copied by these warps in 16-byte pieces; a block whose
+        // keep is negative throughout is left alone
+        if (cls[seq] == 0) {
+          constexpr int kPieces = C / 8;
+          for (int idx = (warp - 4) * 32 + lane; idx < kRowsT * kPieces; idx += 256) {
+            const int64_t r = tile * kRowsT + idx / kPieces;
+            if (r < prm.m) {
+              const int64_t off = r * C + (idx % kPieces) * 8;
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (prm.add_input) v = *reinterpret_cast<const uint4*>(prm.x + off);
+              *reinterpret_cast<uint4*>(prm.out + off) = v;
+            }
+          }
+        }
+        continue;
+      }
       const int xb = ti % XB;
       uint8_t* xt = smem + T::kOffX + xb * T::kTileX;
       constexpr int kHalf = C / 16;   // 8-column pieces of this group's half of the row
@@ -401,6 +457,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         }
         mbar_arrive(&x_free[xb]);  // the store has read the buffer
       }
+      ++ti;
     }
     if (warp == 4 && lane == 0) tma_wait_group<0>();
 #undef CFK_TR_WAIT
@@ -453,6 +510,7 @@ int launch(const TrParams& prm, const void* w1, const void* w2, cudaStream_t st)
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t ntiles = (prm.m + kRowsT - 1) / kRowsT;
   const int grid = int(ntiles < sms ? ntiles : sms);
+  if (prm.keep != nullptr && (ntiles + grid - 1) / grid > kMaxTilesT) return CFK_ERR_UNSUPPORTED;
   transition_kernel<C><<<grid, kThreadsT, T::kSmem, st>>>(tx, tw1, tw2, to, prm);
   return check_launch();
 }
@@ -463,18 +521,19 @@ int launch(const TrParams& prm, const void* w1, const void* w2, cudaStream_t st)
 using namespace cfk;
 
 extern "C" int cfk_transition(const void* x, const float* ln_scale, const float* ln_offset, const void* w1, const void* b1,
-                              const void* w2, const void* b2, void* out, int64_t m, int c, int hdim, float eps,
-                              int add_input, void* stream) {
+                              const void* w2, const void* b2, const void* keep, int keep_dtype, void* out, int64_t m, int c,
+                              int hdim, float eps, int add_input, void* stream) {
   if (!x || !ln_scale || !ln_offset || !w1 || !b1 || !w2 || !b2 || !out) return CFK_ERR_NULL;
   if (m < 0 || hdim <= 0 || hdim % 64 != 0) return CFK_ERR_SHAPE;
   if (c != 128 && c != 256) return CFK_ERR_UNSUPPORTED;
+  if (keep != nullptr && keep_dtype != CFK_F32 && keep_dtype != CFK_BF16) return CFK_ERR_DTYPE;
   if (m == 0) return CFK_OK;
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(out) || !aligned16(b1) || !aligned16(b2) ||
       !aligned16(ln_scale) || !aligned16(ln_offset))
     return CFK_ERR_ALIGN;
   TrParams prm{static_cast<const __nv_bfloat16*>(x), ln_scale, ln_offset, static_cast<const __nv_bfloat16*>(b1),
-               static_cast<const __nv_bfloat16*>(b2), static_cast<__nv_bfloat16*>(out), m, hdim, eps, add_input,
-               device_status_word()};
+               static_cast<const __nv_bfloat16*>(b2), static_cast<__nv_bfloat16*>(out), m, hdim, eps, add_input, keep,
+               keep_dtype, device_status_word()};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   auto st = static_cast<cudaStream_t>(stream);
   return c == 128 ? launch<128>(prm, w1, w2, st) : launch<256>(prm, w1, w2, st);

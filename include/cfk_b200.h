@@ -243,12 +243,15 @@ CFK_API int cfk_transition_hidden(const void* x, const float* ln_scale, const fl
                                   int hdim, float eps, void* stream);
 
 /* The whole LN-MLP transition in one kernel: out = relu(LN(x) w1 + b1) w2 + b2 (+ x); x, out [m,c] bf16 (out may
- * not alias x: rows are re-read for the residual), w1 [c,hdim], b1 [hdim], w2 [hdim,c], b2 [c] bf16; c in {128, 256},
- * hdim a multiple of 64.  Both GEMMs run on the tensor cores and the hidden activation never leaves the chip, as in
- * the reference's kernel.  Replaces fused_transition, transition.py:100-138 (FFI: volta.py:418-428). */
+ * alias x: a 128-row block is read only by the CTA that writes it), w1 [c,hdim], b1 [hdim], w2 [hdim,c], b2 [c] bf16;
+ * c in {128, 256}, hdim a multiple of 64.  keep [m] (CFK_F32 or CFK_BF16) or NULL: a 128-row block whose keep is
+ * nowhere positive is not computed - its rows come out as x (zeros without add_input), and a block whose keep is
+ * negative throughout is left unwritten (transition.py:29-38).  Both GEMMs run on the tensor cores and the hidden
+ * activation never leaves the chip, as in the reference's kernel.  Replaces fused_transition, transition.py:100-138
+ * (FFI: volta.py:418-428). */
 CFK_API int cfk_transition(const void* x, const float* ln_scale, const float* ln_offset, const void* w1, const void* b1,
-                           const void* w2, const void* b2, void* out, int64_t m, int c, int hdim, float eps,
-                           int add_input, void* stream);
+                           const void* w2, const void* b2, const void* keep, int keep_dtype, void* out, int64_t m, int c,
+                           int hdim, float eps, int add_input, void* stream);
 
 /* left, right = mask[m] * (LN(x) lw + lb), mask[m] * (LN(x) rw + rb); x [m,c]; lw, rw [c,k]; k <= 128.
  * Replaces opm_projection, opm.py:36-59. */

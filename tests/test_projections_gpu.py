@@ -206,3 +206,22 @@ def test_transition_keep_leaves_padding_blocks_as_the_reference_does():
     assert torch.equal(out[live.cuda()], full[live.cuda()])
     pad = out[256:640]
     assert torch.equal(pad, x[256:640].cuda()) if add_input else torch.count_nonzero(pad) == 0
+  # a block that is negative throughout is not written at all (transition.py:29-38); at 256 channels too
+  for c2, hd2 in ((128, 512), (256, 1024)):
+    x2, w1b, b1b, w2b, b2b = rnd(rng, 700, c2), rnd(rng, c2, hd2, s=c2 ** -.5), rnd(rng, hd2, s=.1), rnd(rng, hd2, c2, s=hd2 ** -.5), rnd(rng, c2, s=.1)
+    sc2, of2 = 1 + rnd(rng, c2, s=.1).float(), rnd(rng, c2, s=.1).float()
+    keep2 = torch.ones(700)
+    keep2[128:256] = -1
+    keep2[384:512] = 0
+    out = torch.full((700, c2), 7.0, dtype=bf, device="cuda")
+    from colabfold_kernels import _lib
+    dev = [t.cuda().contiguous() for t in (x2, sc2, of2, w1b, b1b, w2b, b2b, keep2)]
+    _lib.call("cfk_transition", *[t.data_ptr() for t in dev[:7]], dev[7].data_ptr(), ops.tag(torch.float32), out.data_ptr(), 700, c2,
+              hd2, 1e-5, 1, torch.cuda.current_stream().cuda_stream)
+    full = ops.transition(*dev[:7], add_input=True)
+    assert bool((out[128:256] == 7.0).all()) and torch.equal(out[384:512], dev[0][384:512])
+    live = torch.ones(700, dtype=torch.bool)
+    live[128:256] = False
+    live[384:512] = False
+    assert torch.equal(out[live.cuda()], full[live.cuda()])
+  assert ops.device_status() == 0
