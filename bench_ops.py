@@ -83,6 +83,7 @@ def make_cases(m, n, c=128):
   x2 = rnd(m2, c2).to(bf)
   ones2, zeros2 = torch.ones(c2, device=dev), torch.zeros(c2, device=dev)
   uw1 = (rnd(c2, 4 * c2) * c2 ** -0.5).to(bf)
+  w4m = (rnd(4, c2, c2) * c2 ** -0.5).to(bf)
   uw2 = (rnd(4 * c2, c2) * (4 * c2) ** -0.5).to(bf)
   ub1, ub2 = torch.zeros(4 * c2, device=dev, dtype=bf), torch.zeros(c2, device=dev, dtype=bf)
   # outer product mean at N_seq 512: projections of the MSA [512, n, 256] and the fused product / mean / output linear
@@ -111,6 +112,8 @@ def make_cases(m, n, c=128):
       "trimul_epilogue": (lambda: ops.trimul_epilogue(x_cm, x, ones, zeros, w, b, w, b, in_scale=ones, in_offset=zeros, add_input=True),
                           3 * m * c * E, 4.0 * m * c * c),
       "ln_projection": (lambda: ops.ln_projection(x, ones, zeros, w4, None), m * c * E + 4 * m * c * E, 2.0 * m * c * 4 * c),
+      "ln_projection_msa": (lambda: ops.ln_projection(x2, ones2, zeros2, w4m, None), m2 * c2 * E + 4 * m2 * c2 * E,
+                            2.0 * m2 * c2 * 4 * c2),
       "ln_head_bias": (lambda: ops.ln_projection(x, ones, zeros, None, wbias), m * c * E + 8 * m * E, 2.0 * m * c * 8),
       "output_projection": (lambda: ops.output_projection(x, w, b, res), 3 * m * c * E, 2.0 * m * c * c),
       "opm_projection": (lambda: ops.opm_projection(x, ones, zeros, lw, lb, lw, lb, mask), m * c * E + 2 * m * 32 * E + m * E,

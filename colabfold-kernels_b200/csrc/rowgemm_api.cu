@@ -149,6 +149,11 @@ extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const flo
   if (m < 0 || g <= 0 || n <= 0 || n % 8 != 0) return CFK_ERR_SHAPE;
   if (!k_ok(a)) return CFK_ERR_UNSUPPORTED;
   if (m == 0) return CFK_OK;
+  if (a == 256 && !f8) {  // the MSA shape has a kernel of its own (128-column chunks)
+    const int rc = ln_proj256_launch(x, ln_scale, ln_offset, w, keep, keep_dtype, p_out, m, g, n, eps,
+                                     static_cast<cudaStream_t>(stream));
+    if (rc != CFK_ERR_UNSUPPORTED) return rc;
+  }
   RowGemmParams prm{};
   prm.src[0] = row_major(x, a, ln_scale, ln_offset);
   prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.eps = eps;

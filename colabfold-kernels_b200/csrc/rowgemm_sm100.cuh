@@ -77,4 +77,9 @@ bool rowgemm_stream_fits(const RowGemmParams& prm);    // room for a two-chunk w
 int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUtensorMap& tw1, cudaStream_t st);
 int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
 
+// LayerNorm -> packed projection at 256 input channels with 128-column chunks (ln_proj256_sm100.cu); returns
+// CFK_ERR_UNSUPPORTED for shapes the general engine should take.
+int ln_proj256_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* w, const void* keep,
+                      int keep_dtype, void* out, int64_t m, int slots, int n, float eps, cudaStream_t st);
+
 }  // namespace cfk

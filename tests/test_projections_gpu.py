@@ -135,7 +135,8 @@ def test_trimul_epilogue(m, c, xdt):
   assert ops.device_status() == 0
 
 
-@pytest.mark.parametrize("m,a,g,n,h", [(4101, 128, 4, 128, 4), (59, 64, 4, 64, 4), (1000, 256, 4, 256, 8), (1, 128, 3, 128, 4)])
+@pytest.mark.parametrize("m,a,g,n,h", [(4101, 128, 4, 128, 4), (59, 64, 4, 64, 4), (1000, 256, 4, 256, 8), (1, 128, 3, 128, 4),
+                                       (40000, 256, 4, 256, 8), (300, 256, 1, 128, 8), (777, 256, 3, 64, 4)])
 def test_ln_projection(m, a, g, n, h):
   from colabfold_kernels import ops
   rng = np.random.default_rng(4)
@@ -147,6 +148,15 @@ def test_ln_projection(m, a, g, n, h):
   chk(p, rp); chk(b, rb)
   p8, _ = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), None, f8=True, f8_scale=0.5)
   assert O.rms_err(p8.cpu().float(), rp * 0.5) <= 5e-2  # tests/test_ln_fusions.py:192
+  if a == 256:  # the 256-channel kernel's own row-block skipping: block 1 unkept (zeros), block 2 negative (unwritten)
+    keep = torch.ones(m)
+    keep[128:256] = 0
+    keep[256:384] = -1
+    pk, _ = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), None, keep=keep.cuda())
+    live = keep > 0
+    assert torch.equal(pk[live.cuda()], p[live.cuda()])
+    assert m <= 128 or float(pk[128:256].float().abs().max()) == 0.0
+    assert ops.device_status() == 0
 
 
 @pytest.mark.parametrize("m,k,c", [(4101, 128, 128), (59, 64, 64), (1000, 256, 256), (1, 128, 256)])
