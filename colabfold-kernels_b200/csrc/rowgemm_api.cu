@@ -100,6 +100,12 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   }
   prm.inner_pad = (prm.inner + pad - 1) / pad * pad;
   prm.eps = eps;
+  if (k == 128 && p == 256 && !fp8) {  // the triangle multiplication's shape has a kernel of its own
+    const int rc = ln_gdp128_launch(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, left, right, prm.outer, prm.inner,
+                                    prm.inner_pad, prm.src[0].stride_outer, prm.src[0].stride_inner, eps,
+                                    static_cast<cudaStream_t>(stream));
+    if (rc != CFK_ERR_UNSUPPORTED) return rc;
+  }
   prm.mode = kModeGdp; prm.dual = 1;
   prm.n_chunk = ci >= 128 ? 128 : 64;
   if (ci % prm.n_chunk != 0) return CFK_ERR_UNSUPPORTED;

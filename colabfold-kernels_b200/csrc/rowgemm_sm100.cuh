@@ -82,4 +82,10 @@ int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
 int ln_proj256_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* w, const void* keep,
                       int keep_dtype, void* out, int64_t m, int slots, int n, float eps, cudaStream_t st);
 
+// LayerNorm -> gated dual projection at 128 channels in and 128 + 128 out, channel-major bf16 (ln_gdp128_sm100.cu);
+// returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.
+int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* wp, const void* bp,
+                     const void* wg, const void* bg, const void* mask, void* left, void* right, int64_t outer, int64_t inner,
+                     int64_t inner_pad, int64_t stride_outer, int64_t stride_inner, float eps, cudaStream_t st);
+
 }  // namespace cfk
