@@ -131,6 +131,12 @@ extern "C" int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void*
   if (!(c == 64 || c == 128) || !k_ok(ca) || (add_input && ca != o)) return CFK_ERR_UNSUPPORTED;
   if (x_cm_dtype != CFK_BF16 && x_cm_dtype != CFK_F32) return CFK_ERR_DTYPE;
   if (m == 0) return CFK_OK;
+  if (c == 128 && ca == 128 && o == 128 && x_cm_dtype == CFK_BF16 && residual == nullptr &&
+      (in_scale == nullptr) == (in_offset == nullptr)) {  // the block's shape has a kernel of its own
+    const int rc = trimul_epi128_launch(x_cm, act, in_scale, in_offset, ln_scale, ln_offset, wo, bo, wg, bg, out, keep,
+                                        keep_dtype, m, eps, add_input, static_cast<cudaStream_t>(stream));
+    if (rc != CFK_ERR_UNSUPPORTED) return rc;
+  }
   RowGemmParams prm{};
   prm.src[0].x = x_cm; prm.src[0].k = c; prm.src[0].channel_major = 1; prm.src[0].dtype = x_cm_dtype;
   prm.src[0].ln_scale = ln_scale; prm.src[0].ln_offset = ln_offset; prm.src[0].stride_outer = 0; prm.src[0].stride_inner = 1;

@@ -88,4 +88,10 @@ int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offse
                      const void* wg, const void* bg, const void* mask, void* left, void* right, int64_t outer, int64_t inner,
                      int64_t inner_pad, int64_t stride_outer, int64_t stride_inner, float eps, cudaStream_t st);
 
+// Triangle-multiplication output at 128 channels with LayerNorm folded around the GEMMs (trimul_epi128_sm100.cu);
+// returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.
+int trimul_epi128_launch(const void* x_cm, const void* act, const float* in_scale, const float* in_offset, const float* ln_scale,
+                         const float* ln_offset, const void* wo, const void* bo, const void* wg, const void* bg, void* out,
+                         const void* keep, int keep_dtype, int64_t m, float eps, int add_input, cudaStream_t st);
+
 }  // namespace cfk
