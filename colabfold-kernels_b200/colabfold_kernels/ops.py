@@ -339,7 +339,7 @@ def transition(x, ln_scale, ln_offset, w1, b1, w2, b2, keep=None, eps=1e-5, add_
   dt = x2.dtype
   m = x2.shape[0]
   kp, kt = _keep(None if keep is None else keep.reshape(-1))
-  if c in (128, 256) and dt == torch.bfloat16:
+  if c in (128, 256) and dt == torch.bfloat16 and hdim % (128 if c == 128 else 64) == 0:
     out = torch.empty_like(x2)  # blocks whose keep is negative throughout stay unwritten, as in the reference
     with torch.cuda.device(x2.device):
       _lib.call("cfk_transition", _ptr(x2), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(w1.to(dt))),

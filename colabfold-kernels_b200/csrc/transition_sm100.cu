@@ -3,14 +3,15 @@
 // registers; here a chunk goes TMEM -> registers -> shared memory and is the A operand of the second GEMM).
 //
 // A persistent CTA walks 128-row tiles of x [M, C].  Per tile:
-//   producer (warp 0)    TMA: the x tile as 64-column K-major atoms; per hidden chunk of 64 columns the weights
-//                        w1[:, chunk] ([C][64], MN-major B) and w2[chunk, :] ([64][C], MN-major B) into two rings
+//   producer (warp 0)    TMA: the x tile as 64-column K-major atoms; per hidden chunk of HC columns (128 at 128
+//                        channels, 64 at 256) the weights w1[:, chunk] ([C][HC], MN-major B) and w2[chunk, :]
+//                        ([HC][C], MN-major B) into two rings
 //   workers (warps 4-11) LayerNorm of the landed tile in place (thread = row, fp32 statistics, bf16 out: the reference
 //                        rounds the normed tile before the dot, transition.py:76-80); per chunk: acc1 -> + b1 -> relu
 //                        -> bf16 -> H tile in shared memory; per tile: acc2 + b2 (+ x) -> out
-//   issuers (warps 1, 2) per chunk n: acc1[n & 1] = LN(x) w1[:, n]  (C / 16 MMAs of N = 64) from warp 1 and
-//                        acc2 += H[n] w2[n, :]  (4 MMAs of N = C) from warp 2
-// TMEM columns: acc1 [0, 64) and [64, 128), acc2 [128, 128 + C).
+//   issuers (warps 1, 2) per chunk n: acc1[n & 1] = LN(x) w1[:, n]  (C / 16 MMAs of N = HC) from warp 1 and
+//                        acc2 += H[n] w2[n, :]  (HC / 16 MMAs of N = C) from warp 2
+// TMEM columns: acc1 [0, HC) and [HC, 2 HC), acc2 [2 HC, 2 HC + C).
 // Every mbarrier wait is deadline-bounded and reports into the status word instead of hanging.
 #include "attention_sm100.cuh"
 
@@ -18,7 +19,6 @@ namespace cfk {
 namespace {
 
 constexpr int kRowsT = 128;   // rows per tile = TMEM lanes
-constexpr int kHC = 64;       // hidden columns per chunk
 constexpr int kMaxTilesT = 768;   // tiles per CTA when row blocks may be skipped
 constexpr int kThreadsT = 384;   // warps 0-3 control, 4-7 and 8-11 two worker groups
 
@@ -26,11 +26,17 @@ template <int C>
 struct TrCfg {
   static constexpr int kAtoms = C / 64;                  // 64-column atoms of an x tile / of a w2 chunk
   static constexpr int kTileX = kRowsT * C * 2;          // x tile
-  static constexpr int kW1 = C * 128;                    // w1 chunk: [C rows][64 columns]
-  static constexpr int kW2 = 64 * C * 2;                 // w2 chunk: kAtoms atoms of [64 rows][64 columns]
-  static constexpr int kH = kRowsT * 128;                // H tile: [128 rows][64 columns]
-  static constexpr int kWRing = C == 128 ? 3 : 2;        // ring depth of each weight ring
-  static constexpr int kHBufs = 2;                       // H buffers: one per worker group
+  // hidden columns per chunk: an N = 64 MMA costs its issue floor, not its tensor time, so 128 wherever the shared
+  // memory allows it (at 256 channels the x tile and the weight chunks leave no room)
+  static constexpr int kHC = C == 128 ? 128 : 64;
+  static constexpr int kGroupsPerChunk = kHC / 64;       // worker groups that share one chunk's epilogue
+  static constexpr int kW1 = C * kHC * 2;                // w1 chunk: kHC / 64 atoms of [C rows][64 columns]
+  static constexpr int kW2 = kHC * C * 2;                // w2 chunk: kAtoms atoms of [kHC rows][64 columns]
+  static constexpr int kH = kRowsT * kHC * 2;            // H tile: kHC / 64 atoms of [128 rows][64 columns]
+  static constexpr int kWRing = 2;                       // ring depth of each weight ring
+  // H buffers: one per worker group when the groups take chunks in turn; one when both work on every chunk (the second
+  // GEMM of a chunk has long completed when the next chunk's activations are ready to be written)
+  static constexpr int kHBufs = kGroupsPerChunk == 2 ? 1 : 2;
   static constexpr int kXBufs = C == 128 ? 2 : 1;        // x tiles in flight
   static constexpr int kOffX = 0;
   static constexpr int kOffW1 = kOffX + kXBufs * kTileX;
@@ -41,7 +47,7 @@ struct TrCfg {
   static constexpr int kOffTmem = kOffBar + kNumBars * 8;
   static constexpr int kOffCls = kOffTmem + 16;           // int8 [kMaxTilesT]: class of each tile this CTA visits
   static constexpr int kSmem = kOffCls + kMaxTilesT + 1024;
-  static constexpr int kColAcc2 = 128;
+  static constexpr int kColAcc2 = 2 * kHC;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kOffW1 % 1024 == 0 && kOffW2 % 1024 == 0 && kOffH % 1024 == 0, "swizzled tiles start on their atom");
 };
@@ -68,7 +74,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
                   const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_out,
                   const TrParams prm) {
   using T = TrCfg<C>;
-  constexpr int WR = T::kWRing, HB = T::kHBufs, XB = T::kXBufs;
+  constexpr int WR = T::kWRing, HB = T::kHBufs, XB = T::kXBufs, kHC = T::kHC, GPC = T::kGroupsPerChunk;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   {
@@ -113,8 +119,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc1_full[i], 1);
-      mbar_init(&acc1_empty[i], 4);
-      mbar_init(&h_full[i], 4);
+      mbar_init(&acc1_empty[i], 4 * GPC);
+      mbar_init(&h_full[i], 4 * GPC);
       mbar_init(&h_empty[i], 1);
     }
     mbar_init(acc2_full, 1);
@@ -194,13 +200,15 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           ok = mbar_wait_deadline(&w1_empty[slot], par);
           if (!ok) { report_timeout(prm.status, 1102); break; }
           mbar_arrive_expect_tx(&w1_full[slot], T::kW1);
-          tma_load_2d(smem + T::kOffW1 + slot * T::kW1, &tm_w1, &w1_full[slot], n * kHC, 0);
+#pragma unroll
+          for (int a = 0; a < kHC / 64; ++a)
+            tma_load_2d(smem + T::kOffW1 + slot * T::kW1 + a * (C * 128), &tm_w1, &w1_full[slot], n * kHC + a * 64, 0);
           ok = mbar_wait_deadline(&w2_empty[slot], par);
           if (!ok) { report_timeout(prm.status, 1103); break; }
           mbar_arrive_expect_tx(&w2_full[slot], T::kW2);
 #pragma unroll
           for (int a = 0; a < T::kAtoms; ++a)
-            tma_load_2d(smem + T::kOffW2 + slot * T::kW2 + a * (64 * 128), &tm_w2, &w2_full[slot], a * 64, n * kHC);
+            tma_load_2d(smem + T::kOffW2 + slot * T::kW2 + a * (kHC * 128), &tm_w2, &w2_full[slot], a * 64, n * kHC);
           // with two buffers the next tile's rows land under this tile's GEMMs
           if (XB == 2 && n == nchunks / 2 && next >= 0) ok = load_x(ti + 1, next);
         }
@@ -228,8 +236,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       constexpr uint32_t idesc2 = make_idesc(kRowsT, C, 1, 1, 0, 1);    // A = H K-major, B = w2 chunk MN-major
       constexpr uint32_t hi128 = desc_hi(1024, kSwz128);
       const uint32_t x_k = desc_lo(smem_u32(smem + T::kOffX), 16);
-      const uint32_t w1_mn = desc_lo(smem_u32(smem + T::kOffW1), 0);
-      const uint32_t w2_mn = desc_lo(smem_u32(smem + T::kOffW2), 64 * 128);  // atoms of 64 columns, 8 KB apart
+      const uint32_t w1_mn = desc_lo(smem_u32(smem + T::kOffW1), C * 128);     // atoms of 64 columns, C * 128 bytes apart
+      const uint32_t w2_mn = desc_lo(smem_u32(smem + T::kOffW2), kHC * 128);   // atoms of 64 columns, kHC * 128 bytes apart
       const uint32_t h_k = desc_lo(smem_u32(smem + T::kOffH), 16);
       bool ok = true;
       uint32_t ti = 0, c1 = 0, c2 = 0;  // tiles done, chunks whose first / second GEMM has been issued
@@ -258,7 +266,8 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         const uint32_t a = h_k + hb * (T::kH >> 4), b = w2_mn + slot * (T::kW2 >> 4);
 #pragma unroll
         for (int kk = 0; kk < kHC / 16; ++kk)
-          mma_f16_ss2(tmem + T::kColAcc2, a + kk * 2, hi128, b + kk * 128, hi128, idesc2, (kk > 0 || !first) ? 1u : 0u);
+          mma_f16_ss2(tmem + T::kColAcc2, a + (kk / 4) * ((kRowsT * 128) >> 4) + (kk % 4) * 2, hi128, b + kk * 128, hi128, idesc2,
+                      (kk > 0 || !first) ? 1u : 0u);
         mma_commit(&w2_empty[slot]);
         mma_commit(&h_empty[hb]);
         ++c2;
@@ -286,9 +295,9 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ workers: two groups of 128 threads, thread = row
-    // of the tile.  Group g normalises and finally writes column half g of the row and owns the chunks n with
-    // (chunks so far + n) % 2 == g, with them acc1[g] and H[g]: the chunk epilogue is a chain of dependent
-    // instructions per warp, so two warps per scheduler hide what one cannot.
+    // of the tile.  Group g normalises and finally writes column half g of the row.  With 64-column chunks it owns the
+    // chunks n with (chunks so far + n) % 2 == g, with them acc1[g] and H[g]; with 128-column chunks it takes column
+    // half g of every chunk.  Either way two warps per scheduler hide the dependent chains one warp cannot.
     const int g = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
@@ -380,13 +389,14 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       // ---- per hidden chunk of this group: relu(acc1 + b1) as bf16 into the H tile (the second GEMM's A operand)
 #pragma unroll 1
       for (int n = 0; n < nchunks; ++n, ++ce) {
-        if (int(ce & 1) != g) continue;
+        if (GPC == 1 && int(ce & 1) != g) continue;   // 64-column chunks: the groups take them in turn
         const int buf = ce & 1, hb = ce % HB;
+        const int coff = GPC == 2 ? g * 64 : 0;       // 128-column chunks: this group's half of every chunk
         CFK_TR_WAIT(&acc1_full[buf], (ce >> 1) & 1, 1302)
         tc_fence_after();
         uint32_t r0[32], r1[32];
-        tmem_ld_x32(tmem + lane_addr + buf * kHC, r0);
-        tmem_ld_x32(tmem + lane_addr + buf * kHC + 32, r1);
+        tmem_ld_x32(tmem + lane_addr + buf * kHC + coff, r0);
+        tmem_ld_x32(tmem + lane_addr + buf * kHC + coff + 32, r1);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -394,7 +404,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         uint32_t hp[32];
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
-          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(prm.b1 + n * kHC + ch * 8));
+          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(prm.b1 + n * kHC + coff + ch * 8));
           const uint32_t bb[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -406,7 +416,7 @@ transition_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         }
         // the second GEMM of the chunk that used this H buffer before has read it
         CFK_TR_WAIT(&h_empty[hb], ((ce / HB) & 1) ^ 1, 1303)
-        uint8_t* ht = smem + T::kOffH + hb * T::kH;
+        uint8_t* ht = smem + T::kOffH + hb * T::kH + (coff / 64) * (kRowsT * 128);
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch)
           *reinterpret_cast<uint4*>(ht + swz_off(row, ch, 128)) = make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
@@ -491,7 +501,7 @@ int launch(const TrParams& prm, const void* w1, const void* w2, cudaStream_t st)
   {
     uint64_t dims[2] = {uint64_t(C), uint64_t(prm.hdim)};
     uint64_t str[1] = {uint64_t(C) * 2};
-    uint32_t box[2] = {64, 64};
+    uint32_t box[2] = {64, uint32_t(T::kHC)};
     int rc = make_tensor_map(&tw2, w2, CFK_BF16, 2, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
@@ -525,6 +535,7 @@ extern "C" int cfk_transition(const void* x, const float* ln_scale, const float*
                               int hdim, float eps, int add_input, void* stream) {
   if (!x || !ln_scale || !ln_offset || !w1 || !b1 || !w2 || !b2 || !out) return CFK_ERR_NULL;
   if (m < 0 || hdim <= 0 || hdim % 64 != 0) return CFK_ERR_SHAPE;
+  if (c == 128 && hdim % 128 != 0) return CFK_ERR_UNSUPPORTED;  // 128-column hidden chunks at 128 channels
   if (c != 128 && c != 256) return CFK_ERR_UNSUPPORTED;
   if (keep != nullptr && keep_dtype != CFK_F32 && keep_dtype != CFK_BF16) return CFK_ERR_DTYPE;
   if (m == 0) return CFK_OK;
