@@ -1,172 +1,275 @@
 // Per-head attention bias from a LayerNorm-ed activation: bias[h, m] = (LN(x) wb)[m, h] (packed_attn.py:225-229).
-// The op reads 2 a bytes per row and writes 2 h (h = 4 or 8 heads): it is HBM-bound on the read, and with so few
-// output columns a tensor-core tile would be all padding, so this is a CUDA-core kernel: a block stages 128 rows in
-// shared memory with coalesced 16-byte loads, then thread = row accumulates, in one pass over its row, the fp32
-// statistics and the dot with up to eight scale-folded weight columns (packed f32x2 FMAs, the weights broadcast from
-// shared memory), and applies mean, rstd and the offset's dot at the end.  The result leaves
-// channel-major: consecutive threads write consecutive rows of one head.
+// The op reads 2 a bytes per row and writes 2 h (h = 4 or 8 heads): it is bound by the read of x.
+//
+// LayerNorm is folded around the dot, LN(x) wb = rstd * (x w' - mean * s) + t with w'[k][h] = scale[k] wb[k][h] (bf16,
+// prepared once per CTA), s[h] = sum_k w'[k][h], t[h] = sum_k offset[k] wb[k][h]: the dot runs on the RAW 128-row tile as TMA
+// lands it (one accumulator of 16 ... 64 columns, a / 16 MMAs per tile), while thread = row takes the row's sum and sum
+// of squares from the same tile, and the epilogue is eight values per thread.  (A CUDA-core version of the dot -
+// thread = row, packed FMAs against weights broadcast from shared memory - spent 1 770 instructions per row and ran at a
+// quarter of the copy bandwidth.)  The result leaves channel-major: consecutive threads write consecutive rows of a head.
 // Row blocks of 128 follow `keep` (transition.py:29-38): a block it marks nowhere is written as zeros, a block that is
-// negative throughout is left unwritten.
-#include "cfk_common.cuh"
-#include "cfk_ptx.cuh"
+// negative throughout is left unwritten.  Every mbarrier wait is deadline-bounded.
+#include "attention_sm100.cuh"
 
 namespace cfk {
 namespace {
 
 constexpr int kRowsHb = 128;
+constexpr int kThreadsHb = 192;     // warp 0 producer, warp 1 MMA issuer, warps 2-5 thread = row
+constexpr int kStagesHb = 3;
+constexpr int kMaxTilesHb = 1024;
+
+struct HbParams {
+  const float* ln_scale;
+  const float* ln_offset;
+  const __nv_bfloat16* wb;   // [a, hp]
+  const void* keep;
+  int keep_dtype;
+  __nv_bfloat16* out;        // [h, m]
+  int64_t m;
+  int h, hp, n;              // n = h rounded up to 16: accumulator columns
+  float eps;
+  int* status;
+};
 
 template <int A>
-__global__ void __launch_bounds__(kRowsHb) ln_head_bias_kernel(const __nv_bfloat16* __restrict__ x,
-                                                               const float* __restrict__ ln_scale,
-                                                               const float* __restrict__ ln_offset,
-                                                               const __nv_bfloat16* __restrict__ wb, const void* keep,
-                                                               int keep_dtype, __nv_bfloat16* __restrict__ out, int64_t m,
-                                                               int h, int hp, float eps) {
-  constexpr int kPitch = A * 2 + 16;             // bytes per staged row: the 16 spare bytes spread the rows over banks
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* xs = smem;                                            // [128][kPitch]
-  float2* ws = reinterpret_cast<float2*>(smem + kRowsHb * kPitch);  // [A][4]: eight weight columns of the current group
-  float2* gb = ws + A * 4;                                       // [A]: LayerNorm scale, offset
-  __shared__ float s_top[kRowsHb / 32], s_sw[8], s_tw[8];
-  const int t = threadIdx.x;
-  for (int k = t; k < A; k += kRowsHb) gb[k] = make_float2(ln_scale[k], ln_offset[k]);
-  // the weights of one group of eight heads in shared memory: w'[k][h] = scale[k] wb[k][h], their column sums and the
-  // offset's dot with wb (one head per thread, the k loop split over 16 threads and combined by shuffle)
-  auto stage_weights = [&](int h0) {
-    for (int i = t; i < A * 4; i += kRowsHb) {
-      const int k = i >> 2, j = (i & 3) * 2 + h0;
-      const float g = gb[k].x;
-      ws[i] = make_float2(j < h ? g * __bfloat162float(wb[k * hp + j]) : 0.f,
-                          j + 1 < h ? g * __bfloat162float(wb[k * hp + j + 1]) : 0.f);
+__global__ void __launch_bounds__(kThreadsHb, 1)
+ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm) {
+  constexpr int kTile = kRowsHb * A * 2;          // A / 64 atoms of [128 rows][64 channels]
+  constexpr int kOffW = kStagesHb * kTile;        // w' as the K-major B operand: A / 64 atoms of [64 rows n][64 channels]
+  constexpr int kWBytes = (A / 64) * 64 * 128;
+  constexpr int kOffCst = kOffW + kWBytes;        // float2 [64]: s, t
+  constexpr int kOffBar = kOffCst + 64 * 8;
+  constexpr int kOffTmem = kOffBar + (2 * kStagesHb + 4 + 1) * 8;
+  constexpr int kOffCls = kOffTmem + 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  {
+    __shared__ int s_abort;
+    if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile int*>(prm.status);
+    __syncthreads();
+    if (s_abort != 0) return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;                     // [3] the tile has landed
+  uint64_t* s_free = full + kStagesHb;       // [3] ... and neither the MMAs nor the row threads read it any more
+  uint64_t* acc_full = s_free + kStagesHb;   // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* w_ready = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  float2* cst = reinterpret_cast<float2*>(smem + kOffCst);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ntiles = (prm.m + kRowsHb - 1) / kRowsHb;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStagesHb; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&s_free[i], 4);
     }
-    {
-      const int hh = t >> 4, part = t & 15;  // 8 heads x 16 threads
-      float sw = 0.f, tw = 0.f;
-      if (h0 + hh < h)
-        for (int k = part; k < A; k += 16) {
-          const float wv = __bfloat162float(wb[k * hp + h0 + hh]);
-          sw = fmaf(gb[k].x, wv, sw);
-          tw = fmaf(gb[k].y, wv, tw);
-        }
-      for (int off = 8; off > 0; off >>= 1) {
-        sw += __shfl_xor_sync(0xffffffffu, sw, off);
-        tw += __shfl_xor_sync(0xffffffffu, tw, off);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(w_ready, 4);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  // tile classes from keep: 1 compute, 0 zeros, -1 leave alone
+  const int8_t* cls = nullptr;
+  if (prm.keep != nullptr) {
+    int8_t* w = reinterpret_cast<int8_t*>(smem + kOffCls);
+    for (int i = warp;; i += kThreadsHb / 32) {
+      const int64_t tile = blockIdx.x + int64_t(i) * gridDim.x;
+      if (tile >= ntiles) break;
+      float top = -1.f;
+      for (int j = lane; j < kRowsHb; j += 32) {
+        const int64_t r = tile * kRowsHb + j;
+        if (r < prm.m)
+          top = fmaxf(top, prm.keep_dtype == CFK_F32 ? static_cast<const float*>(prm.keep)[r]
+                                                     : __bfloat162float(static_cast<const __nv_bfloat16*>(prm.keep)[r]));
       }
-      if (part == 0) {
-        s_sw[hh] = sw;
-        s_tw[hh] = tw;
-      }
+      for (int off = 16; off > 0; off >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+      if (lane == 0) w[i] = top > 0.f ? 1 : (top == 0.f ? 0 : -1);
+    }
+    cls = w;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto next_computed = [&](uint32_t& seq) -> int64_t {
+    for (;; ++seq) {
+      const int64_t tile = blockIdx.x + int64_t(seq) * gridDim.x;
+      if (tile >= ntiles) return -1;
+      if (cls == nullptr || cls[seq] == 1) return tile;
     }
   };
-  __syncthreads();
-  if (h <= 8) stage_weights(0);
-  const int64_t ntiles = (m + kRowsHb - 1) / kRowsHb;
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t r0 = tile * kRowsHb;
-    const int64_t row = r0 + t;
-    // ---- the block's class: largest keep value over its rows (> 0 compute, == 0 zeros, < 0 leave alone)
-    float top = 1.f;
-    if (keep != nullptr) {
-      float v = -1.f;
-      if (row < m)
-        v = keep_dtype == CFK_F32 ? static_cast<const float*>(keep)[row]
-                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(keep)[row]);
-      for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-      if ((t & 31) == 0) s_top[t >> 5] = v;
-      __syncthreads();
-      top = fmaxf(fmaxf(s_top[0], s_top[1]), fmaxf(s_top[2], s_top[3]));
-    }
-    if (top < 0.f) {
-      __syncthreads();
-      continue;
-    }
-    if (top == 0.f) {
-      if (row < m)
-        for (int hh = 0; hh < h; ++hh) out[int64_t(hh) * m + row] = __float2bfloat16_rn(0.f);
-      __syncthreads();
-      continue;
-    }
-    // ---- stage the rows: 16-byte pieces, consecutive threads on consecutive pieces
-    constexpr int kPieces = A / 8;  // per row
-    for (int i = t; i < kRowsHb * kPieces; i += kRowsHb) {
-      const int r = i / kPieces, c = i % kPieces;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (r0 + r < m) v = __ldg(reinterpret_cast<const uint4*>(x + (r0 + r) * A) + c);
-      *reinterpret_cast<uint4*>(xs + r * kPitch + c * 16) = v;
-    }
-    __syncthreads();
-    const uint8_t* mine = xs + t * kPitch;
-    // ---- eight heads at a time, one pass over the row: with w'[k][h] = scale[k] wb[k][h] (fp32, in shared memory)
-    //   (LN(x) wb)[h] = rstd * (sum_k x[k] w'[k][h] - mean * sum_k w'[k][h]) + sum_k offset[k] wb[k][h]
-    // so the dot runs on the raw row while the statistics accumulate beside it (the normalised row is not rounded to
-    // bf16 on the way, which only brings the result closer to exact arithmetic)
-    for (int h0 = 0; h0 < h; h0 += 8) {
-      if (h > 8) {  // more than one group of eight heads: the group's weights are set up per pass
-        __syncthreads();
-        stage_weights(h0);
-        __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t seq = 0, ti = 0;
+      for (int64_t tile = next_computed(seq); tile >= 0 && ok; tile = next_computed(++seq), ++ti) {
+        const int st = ti % kStagesHb;
+        ok = mbar_wait_deadline(&s_free[st], ((ti / kStagesHb) & 1) ^ 1);
+        if (!ok) { report_timeout(prm.status, 1801); break; }
+        mbar_arrive_expect_tx(&full[st], kTile);
+#pragma unroll
+        for (int a = 0; a < A / 64; ++a)
+          tma_load_2d(smem + st * kTile + a * (kRowsHb * 128), &tm_x, &full[st], a * 64, int(tile * kRowsHb));
       }
-      uint64_t acc[4] = {0, 0, 0, 0};
-      float sum = 0.f, sq = 0.f;
-#pragma unroll 2
-      for (int c = 0; c < kPieces; ++c) {
-        const uint4 w = *reinterpret_cast<const uint4*>(mine + c * 16);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer: acc[row][head] = x w'
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(kRowsHb, uint32_t(prm.n), 1, 1, 0, 0);   // both operands K-major
+      constexpr uint32_t hi = desc_hi(1024, kSwz128);
+      const uint32_t wk = desc_lo(smem_u32(smem + kOffW), 16);
+      bool ok = mbar_wait_deadline(w_ready, 0);
+      if (!ok) report_timeout(prm.status, 1802);
+      uint32_t seq = 0, ti = 0;
+      for (int64_t tile = next_computed(seq); tile >= 0 && ok; tile = next_computed(++seq), ++ti) {
+        const int st = ti % kStagesHb, ab = ti & 1;
+        ok = mbar_wait_deadline(&full[st], (ti / kStagesHb) & 1);
+        if (!ok) { report_timeout(prm.status, 1803); break; }
+        ok = mbar_wait_deadline(&acc_empty[ab], ((ti >> 1) & 1) ^ 1);
+        if (!ok) { report_timeout(prm.status, 1804); break; }
+        tc_fence_after();
+        const uint32_t xk = desc_lo(smem_u32(smem + st * kTile), 16);
+#pragma unroll
+        for (int kk = 0; kk < A / 16; ++kk)
+          mma_f16_ss2(tmem + ab * 64, xk + (kk / 4) * ((kRowsHb * 128) >> 4) + (kk % 4) * 2, hi,
+                      wk + (kk / 4) * ((64 * 128) >> 4) + (kk % 4) * 2, hi, idesc, kk > 0);
+        mma_commit(&acc_full[ab]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ row threads
+    const int quad = warp & 3;                      // warps 2-5 -> TMEM lane quarters 2, 3, 0, 1
+    const int trow = quad * 32 + lane;
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    const int pt = (warp - 2) * 32 + lane;
+    bool ok = true;
+    // ---- once: w'[n][k] = scale[k] wb[k][n] as a K-major tile (rows n, 128-byte swizzle), s[n], t[n]
+    for (int i = pt; i < 64 * (A / 8); i += 128) {   // 16-byte pieces: 8 consecutive k of one row n
+      const int n = i / (A / 8), p = i % (A / 8);
+      uint32_t v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int k = p * 8 + 2 * e;
+        const float w0 = n < prm.h ? prm.ln_scale[k] * __bfloat162float(prm.wb[k * prm.hp + n]) : 0.f;
+        const float w1 = n < prm.h ? prm.ln_scale[k + 1] * __bfloat162float(prm.wb[(k + 1) * prm.hp + n]) : 0.f;
+        v[e] = pack_bf16x2(w0, w1);
+      }
+      *reinterpret_cast<uint4*>(smem + kOffW + (p >> 3) * (64 * 128) + swz_off(n, p & 7, 128)) = make_uint4(v[0], v[1], v[2], v[3]);
+    }
+    if (pt < 64) {
+      float s = 0.f, t = 0.f;
+      if (pt < prm.h)
+        for (int k = 0; k < A; ++k) {
+          const float w = __bfloat162float(prm.wb[k * prm.hp + pt]);
+          s += __bfloat162float(__float2bfloat16_rn(prm.ln_scale[k] * w));
+          t = fmaf(prm.ln_offset[k], w, t);
+        }
+      cst[pt] = make_float2(s, t);
+    }
+    fence_proxy_async();
+    named_bar_sync(2, 128);
+    if (lane == 0) mbar_arrive(w_ready);
+
+    uint32_t seq = 0, ti = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++seq) {
+      const int64_t row = tile * kRowsHb + trow;
+      if (cls != nullptr && cls[seq] != 1) {
+        if (cls[seq] == 0 && row < prm.m)
+          for (int hh = 0; hh < prm.h; ++hh) prm.out[int64_t(hh) * prm.m + row] = __float2bfloat16_rn(0.f);
+        continue;
+      }
+      const int st = ti % kStagesHb, ab = ti & 1;
+      if (ok && !mbar_wait_deadline(&full[st], (ti / kStagesHb) & 1)) {
+        report_timeout(prm.status, 1805);
+        ok = false;
+      }
+      // ---- the row's statistics from the raw tile (fp32 sums over bf16 data, one pass)
+      const uint8_t* xs = smem + st * kTile;
+      float s0 = 0.f, s1 = 0.f, q0 = 0.f, q1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < A / 8; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(xs + (c >> 3) * (kRowsHb * 128) + swz_off(trow, c & 7, 128));
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int k = c * 8 + 2 * e;
-          const float y0 = bf16lo_to_f32(ww[e]), y1 = bf16hi_to_f32(ww[e]);
-          sum += y0 + y1;
-          sq = fmaf(y0, y0, fmaf(y1, y1, sq));
-          const uint64_t b0 = f2_pack(y0, y0), b1 = f2_pack(y1, y1);
-          const ulonglong2* w0 = reinterpret_cast<const ulonglong2*>(ws + k * 4);
-          const ulonglong2 p0 = w0[0], p1 = w0[1], q0 = w0[2], q1 = w0[3];
-          acc[0] = f2_fma(b0, p0.x, acc[0]);
-          acc[1] = f2_fma(b0, p0.y, acc[1]);
-          acc[2] = f2_fma(b0, p1.x, acc[2]);
-          acc[3] = f2_fma(b0, p1.y, acc[3]);
-          acc[0] = f2_fma(b1, q0.x, acc[0]);
-          acc[1] = f2_fma(b1, q0.y, acc[1]);
-          acc[2] = f2_fma(b1, q1.x, acc[2]);
-          acc[3] = f2_fma(b1, q1.y, acc[3]);
+          const float a = bf16lo_to_f32(ww[e]), b = bf16hi_to_f32(ww[e]);
+          s0 += a; s1 += b;
+          q0 = fmaf(a, a, q0); q1 = fmaf(b, b, q1);
         }
       }
-      const float mean = sum * (1.0f / A);
-      // second moment about the mean from the raw sums; the row is bf16 data, so fp32 sums leave this difference exact
-      // to far below the data's own precision unless |mean| exceeds the spread a thousandfold
-      const float var = fmaxf(sq * (1.0f / A) - mean * mean, 0.f);
-      const float rstd = rsqrtf(var + eps);
-      if (row < m) {
+      const float mean = (s0 + s1) * (1.0f / A);
+      const float var = fmaxf((q0 + q1) * (1.0f / A) - mean * mean, 0.f);
+      const float rstd = rsqrtf(var + prm.eps);
+      // ---- epilogue: rstd * (acc - mean s) + t, eight heads at a time
+      if (ok && !mbar_wait_deadline(&acc_full[ab], (ti >> 1) & 1)) {
+        report_timeout(prm.status, 1806);
+        ok = false;
+      }
+      tc_fence_after();
+      for (int h0 = 0; h0 < prm.h; h0 += 8) {
+        uint32_t r[8];
+        tmem_ld_x8(tmem + lane_addr + ab * 64 + h0, r);
+        tmem_wait_ld();
+        if (row < prm.m) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float lo, hi;
-          f2_unpack(acc[j], lo, hi);
-          const int ha = h0 + 2 * j;
-          if (ha < h) out[int64_t(ha) * m + row] = __float2bfloat16_rn(fmaf(rstd, lo - mean * s_sw[2 * j], s_tw[2 * j]));
-          if (ha + 1 < h) out[int64_t(ha + 1) * m + row] = __float2bfloat16_rn(fmaf(rstd, hi - mean * s_sw[2 * j + 1], s_tw[2 * j + 1]));
+          for (int j = 0; j < 8; ++j)
+            if (h0 + j < prm.h) {
+              const float2 c = cst[h0 + j];
+              prm.out[int64_t(h0 + j) * prm.m + row] = __float2bfloat16_rn(fmaf(rstd, fmaf(-mean, c.x, __uint_as_float(r[j])), c.y));
+            }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[ab]);
+        mbar_arrive(&s_free[st]);
+      }
+      ++ti;
     }
-    __syncthreads();  // the staged rows are read no more
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
 }
 
 template <int A>
-int launch_hb(const void* x, const float* ln_scale, const float* ln_offset, const void* wb, const void* keep, int keep_dtype,
-              void* out, int64_t m, int h, int hp, float eps, cudaStream_t st) {
-  const int smem = kRowsHb * (A * 2 + 16) + A * 4 * 8 + A * 8;
+int launch_hb(const void* x, const HbParams& prm, cudaStream_t st) {
+  CUtensorMap tx;
+  {
+    uint64_t dims[2] = {uint64_t(A), uint64_t(prm.m)};
+    uint64_t str[1] = {uint64_t(A) * 2};
+    uint32_t box[2] = {64, kRowsHb};
+    int rc = make_tensor_map(&tx, x, CFK_BF16, 2, dims, str, box, 128);
+    if (rc != CFK_OK) return rc;
+  }
+  const int smem = kStagesHb * kRowsHb * A * 2 + (A / 64) * 64 * 128 + 64 * 8 + (2 * kStagesHb + 5) * 8 + 16 + kMaxTilesHb + 1024;
   auto kern = ln_head_bias_kernel<A>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return CFK_ERR_LAUNCH;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int per_sm = 227 * 1024 / (smem + 1024) < 8 ? 227 * 1024 / (smem + 1024) : 8;
-  const int64_t ntiles = (m + kRowsHb - 1) / kRowsHb;
-  const int64_t want = int64_t(sms) * per_sm;
-  const int grid = int(ntiles < want ? ntiles : want);
-  kern<<<grid, kRowsHb, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ln_scale, ln_offset,
-                                    static_cast<const __nv_bfloat16*>(wb), keep, keep_dtype, static_cast<__nv_bfloat16*>(out),
-                                    m, h, hp, eps);
+  const int64_t ntiles = (prm.m + kRowsHb - 1) / kRowsHb;
+  const int grid = int(ntiles < sms ? ntiles : sms);
+  if (prm.keep != nullptr && (ntiles + grid - 1) / grid > kMaxTilesHb) return CFK_ERR_UNSUPPORTED;
+  kern<<<grid, kThreadsHb, smem, st>>>(tx, prm);
   return check_launch();
 }
 
@@ -179,16 +282,18 @@ extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const floa
                                 const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
                                 float eps, void* stream) {
   if (!x || !ln_scale || !ln_offset || !wb || !bias_out) return CFK_ERR_NULL;
-  if (m < 0 || h <= 0 || h > h_padded || h_padded > 64) return CFK_ERR_SHAPE;
+  if (m < 0 || h <= 0 || h > h_padded || h_padded > 64 || m > INT32_MAX) return CFK_ERR_SHAPE;
   if (a != 64 && a != 128 && a != 256) return CFK_ERR_UNSUPPORTED;
   if (keep != nullptr && keep_dtype != CFK_F32 && keep_dtype != CFK_BF16) return CFK_ERR_DTYPE;
   if (m == 0) return CFK_OK;
   if (!aligned16(x)) return CFK_ERR_ALIGN;
-  if (device_status_word() == nullptr) return CFK_ERR_LAUNCH;
+  HbParams prm{ln_scale, ln_offset, static_cast<const __nv_bfloat16*>(wb), keep, keep_dtype,
+               static_cast<__nv_bfloat16*>(bias_out), m, h, h_padded, (h + 15) / 16 * 16, eps, device_status_word()};
+  if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   auto st = static_cast<cudaStream_t>(stream);
   switch (a) {
-    case 64: return launch_hb<64>(x, ln_scale, ln_offset, wb, keep, keep_dtype, bias_out, m, h, h_padded, eps, st);
-    case 128: return launch_hb<128>(x, ln_scale, ln_offset, wb, keep, keep_dtype, bias_out, m, h, h_padded, eps, st);
-    default: return launch_hb<256>(x, ln_scale, ln_offset, wb, keep, keep_dtype, bias_out, m, h, h_padded, eps, st);
+    case 64: return launch_hb<64>(x, prm, st);
+    case 128: return launch_hb<128>(x, prm, st);
+    default: return launch_hb<256>(x, prm, st);
   }
 }
