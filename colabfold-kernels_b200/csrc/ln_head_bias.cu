@@ -15,19 +15,27 @@ namespace cfk {
 namespace {
 
 constexpr int kRowsHb = 128;
-constexpr int kThreadsHb = 192;     // warp 0 producer, warp 1 MMA issuer, warps 2-5 thread = row
+constexpr int kThreadsHb = 320;     // warp 0 producer, warp 1 MMA issuer, warps 2-5 and 6-9: thread = row, tiles in turn
 constexpr int kStagesHb = 3;
 constexpr int kMaxTilesHb = 1024;
 
+// Up to two weight matrices side by side ([a, hp0] giving columns 0 .. h0-1 into out0, [a, hp1] giving h1 more into
+// out1), optional biases, an optional row mask, rows addressed as (outer, inner) with strides so that a transposed read
+// (the MSA with rows running along the depth for a fixed residue) is the same kernel, outputs [h, outer, inner_pad].
 struct HbParams {
   const float* ln_scale;
   const float* ln_offset;
-  const __nv_bfloat16* wb;   // [a, hp]
+  const __nv_bfloat16* w0;   // [a, hp0]
+  const __nv_bfloat16* w1;   // [a, hp1] or null
+  const __nv_bfloat16* b0;   // [h0] or null
+  const __nv_bfloat16* b1;   // [h1] or null
+  const __nv_bfloat16* mask; // per source row, or null; negative counts as zero
   const void* keep;
   int keep_dtype;
-  __nv_bfloat16* out;        // [h, m]
-  int64_t m;
-  int h, hp, n;              // n = h rounded up to 16: accumulator columns
+  __nv_bfloat16* out0;       // [h0, outer, inner_pad]
+  __nv_bfloat16* out1;       // [h1, outer, inner_pad]
+  int64_t outer, inner, inner_pad, stride_outer, stride_inner, tiles_per_outer, ntiles;
+  int h0, hp0, h1, hp1, n;   // n = h0 + h1 rounded up to 16: accumulator columns
   float eps;
   int* status;
 };
@@ -59,7 +67,8 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   float2* cst = reinterpret_cast<float2*>(smem + kOffCst);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t ntiles = (prm.m + kRowsHb - 1) / kRowsHb;
+  const int64_t ntiles = prm.ntiles;
+  const int h = prm.h0 + prm.h1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStagesHb; ++i) {
@@ -70,7 +79,7 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
-    mbar_init(w_ready, 4);
+    mbar_init(w_ready, 8);
     fence_mbar_init();
     tma_prefetch_desc(&tm_x);
   }
@@ -86,11 +95,16 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
       const int64_t tile = blockIdx.x + int64_t(i) * gridDim.x;
       if (tile >= ntiles) break;
       float top = -1.f;
+      const int64_t o = tile / prm.tiles_per_outer, r0 = (tile % prm.tiles_per_outer) * kRowsHb;
       for (int j = lane; j < kRowsHb; j += 32) {
-        const int64_t r = tile * kRowsHb + j;
-        if (r < prm.m)
-          top = fmaxf(top, prm.keep_dtype == CFK_F32 ? static_cast<const float*>(prm.keep)[r]
-                                                     : __bfloat162float(static_cast<const __nv_bfloat16*>(prm.keep)[r]));
+        const int64_t r = r0 + j;
+        if (r < prm.inner) {
+          const int64_t src = o * prm.stride_outer + r * prm.stride_inner;
+          top = fmaxf(top, prm.keep_dtype == CFK_F32 ? static_cast<const float*>(prm.keep)[src]
+                                                     : __bfloat162float(static_cast<const __nv_bfloat16*>(prm.keep)[src]));
+        } else if (r < prm.inner_pad) {
+          top = fmaxf(top, 0.f);
+        }
       }
       for (int off = 16; off > 0; off >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
       if (lane == 0) w[i] = top > 0.f ? 1 : (top == 0.f ? 0 : -1);
@@ -119,9 +133,9 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
         ok = mbar_wait_deadline(&s_free[st], ((ti / kStagesHb) & 1) ^ 1);
         if (!ok) { report_timeout(prm.status, 1801); break; }
         mbar_arrive_expect_tx(&full[st], kTile);
+        const int o = int(tile / prm.tiles_per_outer), r0 = int(tile % prm.tiles_per_outer) * kRowsHb;
 #pragma unroll
-        for (int a = 0; a < A / 64; ++a)
-          tma_load_2d(smem + st * kTile + a * (kRowsHb * 128), &tm_x, &full[st], a * 64, int(tile * kRowsHb));
+        for (int a = 0; a < A / 64; ++a) tma_load_3d(smem + st * kTile + a * (kRowsHb * 128), &tm_x, &full[st], a * 64, r0, o);
       }
     }
     __syncwarp();
@@ -152,46 +166,69 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ row threads
-    const int quad = warp & 3;                      // warps 2-5 -> TMEM lane quarters 2, 3, 0, 1
+    // two groups of four warps take the computed tiles in turn (group = accumulator buffer): a group alone is one warp per
+    // scheduler, and every dependent instruction of its statistics pass and epilogue would wait in the open
+    const int grp = (warp - 2) >> 2;
+    const int quad = warp & 3;                      // TMEM lane quarter of this warp
     const int trow = quad * 32 + lane;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const int pt = (warp - 2) * 32 + lane;
     bool ok = true;
-    // ---- once: w'[n][k] = scale[k] wb[k][n] as a K-major tile (rows n, 128-byte swizzle), s[n], t[n]
-    for (int i = pt; i < 64 * (A / 8); i += 128) {   // 16-byte pieces: 8 consecutive k of one row n
+    // column n of the two weight matrices side by side
+    auto weight = [&](int k, int n) -> float {
+      return __bfloat162float(n < prm.h0 ? prm.w0[k * prm.hp0 + n] : prm.w1[k * prm.hp1 + (n - prm.h0)]);
+    };
+    // ---- once: w'[n][k] = scale[k] w[k][n] as a K-major tile (rows n, 128-byte swizzle), s[n], t[n] (+ bias)
+    for (int i = pt; i < 64 * (A / 8); i += 256) {   // 16-byte pieces: 8 consecutive k of one row n
       const int n = i / (A / 8), p = i % (A / 8);
       uint32_t v[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int k = p * 8 + 2 * e;
-        const float w0 = n < prm.h ? prm.ln_scale[k] * __bfloat162float(prm.wb[k * prm.hp + n]) : 0.f;
-        const float w1 = n < prm.h ? prm.ln_scale[k + 1] * __bfloat162float(prm.wb[(k + 1) * prm.hp + n]) : 0.f;
-        v[e] = pack_bf16x2(w0, w1);
+        v[e] = pack_bf16x2(n < h ? prm.ln_scale[k] * weight(k, n) : 0.f, n < h ? prm.ln_scale[k + 1] * weight(k + 1, n) : 0.f);
       }
       *reinterpret_cast<uint4*>(smem + kOffW + (p >> 3) * (64 * 128) + swz_off(n, p & 7, 128)) = make_uint4(v[0], v[1], v[2], v[3]);
     }
     if (pt < 64) {
       float s = 0.f, t = 0.f;
-      if (pt < prm.h)
+      if (pt < h) {
         for (int k = 0; k < A; ++k) {
-          const float w = __bfloat162float(prm.wb[k * prm.hp + pt]);
+          const float w = weight(k, pt);
           s += __bfloat162float(__float2bfloat16_rn(prm.ln_scale[k] * w));
           t = fmaf(prm.ln_offset[k], w, t);
         }
+        if (pt < prm.h0 && prm.b0 != nullptr) t += __bfloat162float(prm.b0[pt]);
+        if (pt >= prm.h0 && prm.b1 != nullptr) t += __bfloat162float(prm.b1[pt - prm.h0]);
+      }
       cst[pt] = make_float2(s, t);
     }
     fence_proxy_async();
-    named_bar_sync(2, 128);
+    named_bar_sync(2, 256);
     if (lane == 0) mbar_arrive(w_ready);
 
+    const int64_t plane = prm.outer * prm.inner_pad;
+    // where column n of the accumulator goes
+    auto dst = [&](int n, int64_t at) -> __nv_bfloat16* {
+      return n < prm.h0 ? prm.out0 + int64_t(n) * plane + at : prm.out1 + int64_t(n - prm.h0) * plane + at;
+    };
     uint32_t seq = 0, ti = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++seq) {
-      const int64_t row = tile * kRowsHb + trow;
+      const int64_t o = tile / prm.tiles_per_outer;
+      const int64_t r = (tile % prm.tiles_per_outer) * kRowsHb + trow;
+      const bool in_pad = r < prm.inner_pad;          // a position of the output
+      const bool valid = r < prm.inner;               // ... that is a row of x
+      const int64_t at = o * prm.inner_pad + r;
       if (cls != nullptr && cls[seq] != 1) {
-        if (cls[seq] == 0 && row < prm.m)
-          for (int hh = 0; hh < prm.h; ++hh) prm.out[int64_t(hh) * prm.m + row] = __float2bfloat16_rn(0.f);
+        if (cls[seq] == 0 && in_pad && grp == int(seq & 1))
+          for (int hh = 0; hh < h; ++hh) *dst(hh, at) = __float2bfloat16_rn(0.f);
         continue;
       }
+      if (int(ti & 1) != grp) {  // the other group's tile
+        ++ti;
+        continue;
+      }
+      float mk = valid ? 1.f : 0.f;
+      if (valid && prm.mask != nullptr) mk = fmaxf(__bfloat162float(prm.mask[o * prm.stride_outer + r * prm.stride_inner]), 0.f);
       const int st = ti % kStagesHb, ab = ti & 1;
       if (ok && !mbar_wait_deadline(&full[st], (ti / kStagesHb) & 1)) {
         report_timeout(prm.status, 1805);
@@ -220,17 +257,21 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
         ok = false;
       }
       tc_fence_after();
-      for (int h0 = 0; h0 < prm.h; h0 += 8) {
-        uint32_t r[8];
-        tmem_ld_x8(tmem + lane_addr + ab * 64 + h0, r);
+      const float nmr = -mean * rstd * mk, rm = rstd * mk;   // mk * (rstd * (acc - mean s) + t) = rm acc + nmr s + mk t
+      for (int hb = 0; hb < h; hb += 16) {
+        uint32_t acc[16];
+        tmem_ld_x16(tmem + lane_addr + ab * 64 + hb, acc);
         tmem_wait_ld();
-        if (row < prm.m) {
+        if (in_pad) {
+          __nv_bfloat16* p = hb < prm.h0 ? prm.out0 + int64_t(hb) * plane + at : prm.out1 + int64_t(hb - prm.h0) * plane + at;
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (h0 + j < prm.h) {
-              const float2 c = cst[h0 + j];
-              prm.out[int64_t(h0 + j) * prm.m + row] = __float2bfloat16_rn(fmaf(rstd, fmaf(-mean, c.x, __uint_as_float(r[j])), c.y));
+          for (int j = 0; j < 16; ++j) {
+            if (hb + j == prm.h0) p = prm.out1 - int64_t(j) * plane + at;   // the second output starts here
+            if (hb + j < h) {
+              const float2 c = cst[hb + j];
+              p[int64_t(j) * plane] = __float2bfloat16_rn(fmaf(rm, __uint_as_float(acc[j]), fmaf(nmr, c.x, mk * c.y)));
             }
+          }
         }
       }
       tc_fence_before();
@@ -251,13 +292,21 @@ ln_head_bias_kernel(const __grid_constant__ CUtensorMap tm_x, const HbParams prm
 }
 
 template <int A>
-int launch_hb(const void* x, const HbParams& prm, cudaStream_t st) {
+int launch_hb(const void* x, HbParams prm, cudaStream_t st) {
+  prm.tiles_per_outer = (prm.inner_pad + kRowsHb - 1) / kRowsHb;
+  prm.ntiles = prm.outer * prm.tiles_per_outer;
+  prm.n = (prm.h0 + prm.h1 + 15) / 16 * 16;
+  prm.status = device_status_word();
+  if (prm.status == nullptr) return CFK_ERR_LAUNCH;
+  if (prm.ntiles == 0) return CFK_OK;
   CUtensorMap tx;
   {
-    uint64_t dims[2] = {uint64_t(A), uint64_t(prm.m)};
-    uint64_t str[1] = {uint64_t(A) * 2};
-    uint32_t box[2] = {64, kRowsHb};
-    int rc = make_tensor_map(&tx, x, CFK_BF16, 2, dims, str, box, 128);
+    const uint64_t row = uint64_t(A) * 2;
+    uint64_t dims[3] = {uint64_t(A), uint64_t(prm.inner), uint64_t(prm.outer)};
+    uint64_t str[2] = {uint64_t(prm.stride_inner) * row,
+                       (prm.outer > 1 ? uint64_t(prm.stride_outer) : uint64_t(prm.inner) * uint64_t(prm.stride_inner)) * row};
+    uint32_t box[3] = {64, kRowsHb, 1};
+    int rc = make_tensor_map(&tx, x, CFK_BF16, 3, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
   const int smem = kStagesHb * kRowsHb * A * 2 + (A / 64) * 64 * 128 + 64 * 8 + (2 * kStagesHb + 5) * 8 + 16 + kMaxTilesHb + 1024;
@@ -266,11 +315,19 @@ int launch_hb(const void* x, const HbParams& prm, cudaStream_t st) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t ntiles = (prm.m + kRowsHb - 1) / kRowsHb;
-  const int grid = int(ntiles < sms ? ntiles : sms);
-  if (prm.keep != nullptr && (ntiles + grid - 1) / grid > kMaxTilesHb) return CFK_ERR_UNSUPPORTED;
+  const int grid = int(prm.ntiles < sms ? prm.ntiles : sms);
+  if (prm.keep != nullptr && (prm.ntiles + grid - 1) / grid > kMaxTilesHb) return CFK_ERR_UNSUPPORTED;
   kern<<<grid, kThreadsHb, smem, st>>>(tx, prm);
   return check_launch();
+}
+
+int launch_hb_any(const void* x, int a, const HbParams& prm, cudaStream_t st) {
+  switch (a) {
+    case 64: return launch_hb<64>(x, prm, st);
+    case 128: return launch_hb<128>(x, prm, st);
+    case 256: return launch_hb<256>(x, prm, st);
+    default: return CFK_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace
@@ -282,18 +339,41 @@ extern "C" int cfk_ln_head_bias(const void* x, const float* ln_scale, const floa
                                 const void* keep, int keep_dtype, void* bias_out, int64_t m, int a, int h, int h_padded,
                                 float eps, void* stream) {
   if (!x || !ln_scale || !ln_offset || !wb || !bias_out) return CFK_ERR_NULL;
-  if (m < 0 || h <= 0 || h > h_padded || h_padded > 64 || m > INT32_MAX) return CFK_ERR_SHAPE;
+  if (m < 0 || h <= 0 || h > h_padded || h > 64 || m > INT32_MAX) return CFK_ERR_SHAPE;
   if (a != 64 && a != 128 && a != 256) return CFK_ERR_UNSUPPORTED;
   if (keep != nullptr && keep_dtype != CFK_F32 && keep_dtype != CFK_BF16) return CFK_ERR_DTYPE;
   if (m == 0) return CFK_OK;
   if (!aligned16(x)) return CFK_ERR_ALIGN;
-  HbParams prm{ln_scale, ln_offset, static_cast<const __nv_bfloat16*>(wb), keep, keep_dtype,
-               static_cast<__nv_bfloat16*>(bias_out), m, h, h_padded, (h + 15) / 16 * 16, eps, device_status_word()};
-  if (prm.status == nullptr) return CFK_ERR_LAUNCH;
-  auto st = static_cast<cudaStream_t>(stream);
-  switch (a) {
-    case 64: return launch_hb<64>(x, prm, st);
-    case 128: return launch_hb<128>(x, prm, st);
-    default: return launch_hb<256>(x, prm, st);
-  }
+  HbParams prm{};
+  prm.ln_scale = ln_scale; prm.ln_offset = ln_offset;
+  prm.w0 = static_cast<const __nv_bfloat16*>(wb); prm.h0 = h; prm.hp0 = h_padded;
+  prm.keep = keep; prm.keep_dtype = keep_dtype;
+  prm.out0 = static_cast<__nv_bfloat16*>(bias_out);
+  prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.stride_outer = 0; prm.stride_inner = 1;
+  prm.eps = eps;
+  return launch_hb_any(x, a, prm, static_cast<cudaStream_t>(stream));
+}
+
+// The two outer-product-mean projections written channel-major with the MSA depth contiguous, [k, r, pitch]: x [s, r, c]
+// is read with rows running along s for a fixed residue, so that the fused outer product mean takes both results as
+// K-major operands without a transposed copy.
+extern "C" int cfk_opm_projection_cm(const void* x, const float* ln_scale, const float* ln_offset, const void* lw,
+                                     const void* lb, const void* rw, const void* rb, const void* mask, void* left,
+                                     void* right, int64_t s, int64_t r, int c, int k, int64_t pitch, float eps,
+                                     void* stream) {
+  if (!x || !ln_scale || !ln_offset || !lw || !lb || !rw || !rb || !mask || !left || !right) return CFK_ERR_NULL;
+  if (s < 0 || r < 0 || k <= 0 || k > 32 || pitch < s || s > INT32_MAX || r > INT32_MAX) return CFK_ERR_SHAPE;
+  if (c != 64 && c != 128 && c != 256) return CFK_ERR_UNSUPPORTED;
+  if (s == 0 || r == 0) return CFK_OK;
+  if (!aligned16(x)) return CFK_ERR_ALIGN;
+  HbParams prm{};
+  prm.ln_scale = ln_scale; prm.ln_offset = ln_offset;
+  prm.w0 = static_cast<const __nv_bfloat16*>(lw); prm.h0 = k; prm.hp0 = k;
+  prm.w1 = static_cast<const __nv_bfloat16*>(rw); prm.h1 = k; prm.hp1 = k;
+  prm.b0 = static_cast<const __nv_bfloat16*>(lb); prm.b1 = static_cast<const __nv_bfloat16*>(rb);
+  prm.mask = static_cast<const __nv_bfloat16*>(mask);
+  prm.out0 = static_cast<__nv_bfloat16*>(left); prm.out1 = static_cast<__nv_bfloat16*>(right);
+  prm.outer = r; prm.inner = s; prm.inner_pad = pitch; prm.stride_outer = 1; prm.stride_inner = r;
+  prm.eps = eps;
+  return launch_hb_any(x, c, prm, static_cast<cudaStream_t>(stream));
 }

@@ -240,28 +240,3 @@ extern "C" int cfk_opm_projection(const void* x, const float* ln_scale, const fl
   return run_chunks(prm, 1, lw, rw, 1, k, static_cast<cudaStream_t>(stream));
 }
 
-// The same two projections written channel-major with the MSA depth contiguous, [k, r, pitch]: x [s, r, c] is read
-// with rows running along s for a fixed residue (as the pair is read transposed for incoming edges), so that the fused
-// outer product mean takes both results as K-major operands without a transposed copy.
-extern "C" int cfk_opm_projection_cm(const void* x, const float* ln_scale, const float* ln_offset, const void* lw,
-                                     const void* lb, const void* rw, const void* rb, const void* mask, void* left,
-                                     void* right, int64_t s, int64_t r, int c, int k, int64_t pitch, float eps,
-                                     void* stream) {
-  if (!x || !ln_scale || !ln_offset || !lw || !lb || !rw || !rb || !mask || !left || !right) return CFK_ERR_NULL;
-  if (s < 0 || r < 0 || k <= 0 || k % 8 != 0 || k > 64 || pitch < s) return CFK_ERR_SHAPE;
-  if (pitch % 8 != 0) return CFK_ERR_ALIGN;
-  if (!k_ok(c)) return CFK_ERR_UNSUPPORTED;
-  if (s == 0 || r == 0) return CFK_OK;
-  RowGemmParams prm{};
-  prm.src[0] = row_major(x, c, ln_scale, ln_offset);
-  prm.outer = r; prm.inner = s; prm.src[0].stride_outer = 1; prm.src[0].stride_inner = r;
-  prm.inner_pad = pitch; prm.eps = eps;
-  prm.mode = kModeLinear; prm.dual = 1;
-  prm.n_chunk = 64;
-  prm.chunks_per_slot = 1; prm.chunks_per_array = 1;
-  prm.bias[0] = lb; prm.bias[1] = rb; prm.bias_len = k;
-  prm.rowmask = mask; prm.rowmask_dtype = CFK_BF16;
-  prm.out[0] = left; prm.out[1] = right; prm.ldo = k; prm.n_valid = k; prm.out_dtype = CFK_BF16; prm.out_scale = 1.f;
-  prm.out_channel_major = 1;
-  return run_chunks(prm, 1, lw, rw, 1, k, static_cast<cudaStream_t>(stream));
-}

@@ -1012,7 +1012,6 @@ int launch_rowgemm(const RowGemmParams& prm, const CUtensorMap& tw0, const CUten
   CFK_RG_VARIANT(kModeLinear, 0, 0, 2, 1, 1, 1)
   // two projections of one normed tile (outer-product-mean projection)
   CFK_RG_VARIANT(kModeLinear, 1, 0, 0, 0, 0, 1)
-  CFK_RG_VARIANT(kModeLinear, 1, 0, 1, 0, 0, 1)
   CFK_RG_VARIANT(kModeLinear, 1, 0, 2, 0, 0, 1)
 #undef CFK_RG_VARIANT
   if (rc != CFK_OK) return rc;

@@ -260,7 +260,7 @@ CFK_API int cfk_opm_projection(const void* x, const float* ln_scale, const float
                                void* right, int64_t m, int c, int k, float eps, void* stream);
 
 /* The same two projections written channel-major with the MSA depth contiguous: x [s,r,c], mask [s,r] ->
- * left, right [k, r, pitch] (pitch >= s, a multiple of 8; columns s..pitch-1 are zeros); k <= 64.  This is the operand
+ * left, right [k, r, pitch] (pitch >= s, a multiple of 8; columns s..pitch-1 are zeros); k <= 32.  This is the operand
  * layout of cfk_opm_fused.  The reference's opm_projection (opm.py:36-59) writes [s,r,k]; the layout is internal to
  * the deep outer product mean. */
 CFK_API int cfk_opm_projection_cm(const void* x, const float* ln_scale, const float* ln_offset, const void* lw,
