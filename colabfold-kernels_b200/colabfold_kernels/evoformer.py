@@ -155,13 +155,54 @@ class CollectiveTimeout(RuntimeError):
   """A collective of the sharded block did not complete in time (a peer is missing or stuck)."""
 
 
+class PeerExchange:
+  """All-to-all over NVLink peer memory for the sharded block: receive buffers and flags in symmetric memory
+  (torch.distributed._symmetric_memory supplies the allocation and the exchange of device pointers, nothing else),
+  the transfers and the barrier are kernels of the library (cfk_peer_alltoall: plain stores into the peers' buffers, a
+  flag barrier with a bounded wait).  Every call site of the block has its own receive buffer, allocated the first time
+  the site runs (a collective rendezvous: run the block once eagerly before recording it into a CUDA graph); what a site
+  received stays valid until the same site runs again."""
+
+  def __init__(self, group, device):
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+    self.symm, self.group, self.device = symm, group if group is not None else dist.group.WORLD, device
+    self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
+    self.flags = symm.empty(64, dtype=torch.int32, device=device)
+    self.flags.zero_()
+    torch.cuda.synchronize(device)
+    self._handles = [symm.rendezvous(self.flags, self.group)]
+    self.flag_ptrs = torch.tensor([int(p) for p in self._handles[0].buffer_ptrs], dtype=torch.int64, device=device)
+    self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+    self.sites = {}
+    dist.barrier(group)  # every rank's flags are zero before any peer counts on them
+
+  def _site(self, site, nbytes):
+    if site not in self.sites or self.sites[site][0].numel() < nbytes:
+      buf = self.symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+      h = self.symm.rendezvous(buf, self.group)
+      self._handles.append(h)
+      self.sites[site] = (buf, torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=self.device))
+    return self.sites[site]
+
+  def all_to_all(self, site, x):
+    """x [P, ...] contiguous: part p goes to rank p -> [P, ...] with part q what rank q sent here (a view of the site's
+    receive buffer)."""
+    from colabfold_kernels import ops
+    nbytes = x.numel() * x.element_size()
+    buf, ptrs = self._site(site, nbytes)
+    ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, self.P)
+    return buf[:nbytes].view(x.dtype).view(x.shape)
+
+
 class ShardedBlock:
   """The same block with the MSA sharded over sequences and the pair over rows, one rank per GPU.
 
   Inputs and outputs of `__call__` are the local shards msa [s/P, r, c_m] and pair [r/P, r, c_z]; the masks are
   replicated.  s and r must be divisible by the world size."""
 
-  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False, fp8_opm=False, exchange_triangle=None):
+  def __init__(self, K, params, group=None, fp8_trimul=False, fp8_attention=False, fp8_opm=False, exchange_triangle=None,
+               peer_exchange=None):
     import torch.distributed as dist
     self.exchange_triangle = exchange_triangle  # None: by rank count; True / False: force the exchanged / gathered form
     self.K, self.params, self.dist, self.group = K, params, dist, group
@@ -170,24 +211,34 @@ class ShardedBlock:
     self.fo = {"fp8": True} if fp8_opm else {}  # e4m3 outer product of the MSA projections
     self.P = dist.get_world_size(group)
     self.rank = dist.get_rank(group)
+    # a PeerExchange: the all-to-alls run as the library's kernels over NVLink peer memory instead of NCCL's
+    self.peer, self._site_no = peer_exchange, 0
+
+  def _all_to_all(self, send):
+    """send [P, ...] contiguous -> what every rank sent here, [P, ...]."""
+    self._site_no += 1
+    if self.peer is not None:
+      return self.peer.all_to_all(self._site_no, send)
+    recv = torch.empty_like(send)
+    if send.element_size() == 1:  # e4m3 operands travel as bytes
+      self.dist.all_to_all_single(recv.view(torch.uint8), send.view(torch.uint8), group=self.group)
+    else:
+      self.dist.all_to_all_single(recv, send, group=self.group)
+    return recv
 
   # dim 0 sharded -> dim 1 sharded: [n0/P, n1, c] -> [n0, n1/P, c]
   def rows_to_cols(self, x):
     P = self.P
     n0, n1, c = x.shape
     send = x.reshape(n0, P, n1 // P, c).permute(1, 0, 2, 3).contiguous()
-    recv = torch.empty_like(send)
-    self.dist.all_to_all_single(recv, send, group=self.group)
-    return recv.reshape(P * n0, n1 // P, c)
+    return self._all_to_all(send).reshape(P * n0, n1 // P, c)
 
   # dim 1 sharded -> dim 0 sharded: [n0, n1/P, c] -> [n0/P, n1, c]
   def cols_to_rows(self, x):
     P = self.P
     n0, n1, c = x.shape
     send = x.reshape(P, n0 // P, n1, c).contiguous()
-    recv = torch.empty_like(send)
-    self.dist.all_to_all_single(recv, send, group=self.group)
-    return recv.permute(1, 0, 2, 3).reshape(n0 // P, P * n1, c)
+    return self._all_to_all(send).permute(1, 0, 2, 3).reshape(n0 // P, P * n1, c)
 
   def gather(self, x, dim):
     x = x.contiguous()
@@ -207,12 +258,7 @@ class ShardedBlock:
 
   def exchange(self, x):
     """All-to-all of x [P, ...] along its leading axis (part p goes to rank p), no re-layout on either side."""
-    recv = torch.empty_like(x)
-    if x.element_size() == 1:  # e4m3 operands travel as bytes
-      self.dist.all_to_all_single(recv.view(torch.uint8), x.view(torch.uint8), group=self.group)
-    else:
-      self.dist.all_to_all_single(recv, x, group=self.group)
-    return recv
+    return self._all_to_all(x.contiguous())
 
   def triangle_product(self, a, b, split_k):
     """x_cm [c, rows/P, r] of a triangle multiplication from this rank's channel-major operands, or None when the
@@ -287,6 +333,7 @@ class ShardedBlock:
 
   def __call__(self, msa_s, pair_r, msa_mask, pair_mask):
     self.validate(msa_s, pair_r, msa_mask, pair_mask)
+    self._site_no = 0
     K, prm, d = self.K, self.params, self.params["d_head"]
     s, r = msa_mask.shape
     ss, rs = self.shard(s), self.shard(r)

@@ -157,6 +157,16 @@ def _packed_attention_qk8(p, p8, bias, kmask, gate_bias, column, trim, want_lse)
   return (out, lse) if want_lse else out
 
 
+# ------------------------------------------------------------------------------------------ peer all-to-all
+def peer_alltoall(send, recv_ptrs, flag_ptrs, counter, rank, parts):
+  """Part p of send [parts, ...] into rank p's receive buffer (device pointers in recv_ptrs), then the flag barrier."""
+  send = _c(send)
+  chunk = send.numel() * send.element_size() // parts
+  with torch.cuda.device(send.device):
+    _lib.call("cfk_peer_alltoall", _ptr(send), _ptr(recv_ptrs), _ptr(flag_ptrs), _ptr(counter), int(rank), int(parts), chunk,
+              _stream())
+
+
 # ------------------------------------------------------------------------------------------ contraction
 def contract(a, b, alpha=1.0):
   """out[c,i,j] = alpha * sum_k a[c,i,k] b[c,j,k]; a, b bf16 or float8_e4m3fn -> bf16."""

@@ -1,0 +1,91 @@
+// All-to-all over NVLink peer memory with the library's own kernels: plain 16-byte stores into the peers' receive
+// buffers (no TMA, no multicast) and a flag barrier with bounded waits.  For the row-sharded Evoformer block, whose
+// operands switch between row and column sharding (and, for the triangle multiplication, to channel shards and back)
+// ten times per block: an NCCL all-to-all of 33-67 MB per rank reaches a third of the link rate there.
+//
+// The receive buffers and the flag array live in symmetric memory (same allocation on every rank, each rank holding
+// the others' device pointers); nothing here allocates or synchronises the host.
+#include "cfk_common.cuh"
+
+namespace cfk {
+namespace {
+
+// part p of `send` ([parts][chunk] bytes) goes to rank p, where it lands as part `rank` of that rank's receive buffer
+__global__ void __launch_bounds__(256) peer_alltoall_kernel(const uint4* __restrict__ send, void* const* __restrict__ recv_ptrs,
+                                                            int rank, int parts, int64_t chunk16, int blocks_per_part) {
+  const int p = blockIdx.x / blocks_per_part, b = blockIdx.x % blocks_per_part;
+  // start with the next rank so that the ranks do not all write to the same peer at the same time
+  const int peer = (rank + 1 + p) % parts;
+  const uint4* src = send + int64_t(peer) * chunk16;
+  uint4* dst = static_cast<uint4*>(recv_ptrs[peer]) + int64_t(rank) * chunk16;
+  const int64_t stride = int64_t(blocks_per_part) * blockDim.x;
+  int64_t i = int64_t(b) * blockDim.x + threadIdx.x;
+  // four independent 16-byte transfers in flight per thread
+  for (; i + 3 * stride < chunk16; i += 4 * stride) {
+    const uint4 v0 = src[i], v1 = src[i + stride], v2 = src[i + 2 * stride], v3 = src[i + 3 * stride];
+    dst[i] = v0;
+    dst[i + stride] = v1;
+    dst[i + 2 * stride] = v2;
+    dst[i + 3 * stride] = v3;
+  }
+  for (; i < chunk16; i += stride) dst[i] = src[i];
+}
+
+// Every rank tells every other that all it sent before this point has been written, then waits for the same from all.
+// flags[r] is rank r's array of `parts` counters; counter[0] on this device numbers the barriers (it lives on the device
+// so that a replayed CUDA graph counts on).  One thread per peer.
+__global__ void peer_barrier_kernel(int* const* __restrict__ flag_ptrs, int* __restrict__ counter, int rank, int parts,
+                                    int* status, int code) {
+  __shared__ int s_epoch;
+  if (threadIdx.x == 0) s_epoch = *counter + 1;
+  __syncthreads();
+  const int epoch = s_epoch;
+  const int p = threadIdx.x;
+  if (p < parts) {
+    __threadfence_system();  // the data stores of the kernels before this one are ordered before the flag
+    int* theirs = flag_ptrs[p] + rank;
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(theirs), "r"(epoch) : "memory");
+    const int* mine = flag_ptrs[rank] + p;
+    const long long t0 = clock64();
+    bool ok = false;
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (v - epoch >= 0) { ok = true; break; }
+      if (clock64() - t0 > (1ll << 31)) break;   // about a second: a peer is missing
+    }
+    if (!ok) report_timeout(status, code);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = epoch;
+}
+
+}  // namespace
+}  // namespace cfk
+
+using namespace cfk;
+
+extern "C" int cfk_peer_alltoall(const void* send, const void* recv_ptrs, const void* flag_ptrs, void* counter, int rank,
+                                 int parts, int64_t chunk_bytes, void* stream) {
+  if (!send || !recv_ptrs || !flag_ptrs || !counter) return CFK_ERR_NULL;
+  if (parts < 1 || parts > 32 || rank < 0 || rank >= parts || chunk_bytes < 0) return CFK_ERR_SHAPE;
+  if (chunk_bytes % 16 != 0 || !aligned16(send)) return CFK_ERR_ALIGN;
+  int* status = device_status_word();
+  if (status == nullptr) return CFK_ERR_LAUNCH;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (chunk_bytes > 0) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int bpp = (2 * sms + parts - 1) / parts;   // about two blocks per SM in all
+    const int64_t chunk16 = chunk_bytes / 16;
+    if (int64_t(bpp) * 256 > chunk16) bpp = int((chunk16 + 255) / 256);
+    if (bpp < 1) bpp = 1;
+    peer_alltoall_kernel<<<bpp * parts, 256, 0, st>>>(static_cast<const uint4*>(send), static_cast<void* const*>(recv_ptrs), rank,
+                                                      parts, chunk16, bpp);
+    int rc = check_launch();
+    if (rc != CFK_OK) return rc;
+  }
+  peer_barrier_kernel<<<1, 32, 0, st>>>(static_cast<int* const*>(flag_ptrs), static_cast<int*>(counter), rank, parts, status, 1901);
+  return check_launch();
+}

@@ -20,7 +20,7 @@ def _inputs(s=64, r=256):
   return msa.bfloat16(), pair.bfloat16(), msa_mask, pair_mask
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, peer=False):
   for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
     sys.path.insert(0, p)
   from colabfold_kernels import evoformer, ops
@@ -30,9 +30,14 @@ def _worker(rank, world, port, out):
   dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
   msa, pair, msa_mask, pair_mask = _inputs()
   params = evoformer.init_params(seed=1, device=dev)
-  blk = evoformer.ShardedBlock(evoformer.cuda_kernels(), params)
+  # peer: the all-to-alls as the library's kernels over NVLink peer memory (and the triangle multiplication in its
+  # exchanged form, so that every kind of all-to-all of the block runs); twice, so that receive buffers and the barrier
+  # counter are reused
+  kw = dict(exchange_triangle=True, peer_exchange=evoformer.PeerExchange(None, dev)) if peer else {}
+  blk = evoformer.ShardedBlock(evoformer.cuda_kernels(), params, **kw)
   s, r = msa_mask.shape
-  m, p = blk(msa[blk.shard(s)].to(dev), pair[blk.shard(r)].to(dev), msa_mask.to(dev), pair_mask.to(dev))
+  for _ in range(2 if peer else 1):
+    m, p = blk(msa[blk.shard(s)].to(dev), pair[blk.shard(r)].to(dev), msa_mask.to(dev), pair_mask.to(dev))
   torch.cuda.synchronize()
   torch.save((m.cpu(), p.cpu(), ops.device_status()), os.path.join(out, f"rank{rank}.pt"))
   dist.barrier()
@@ -40,12 +45,13 @@ def _worker(rank, world, port, out):
 
 
 @pytest.mark.timeout(600)
-def test_two_gpu_block_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("peer", [False, True])
+def test_two_gpu_block_matches_single_gpu(tmp_path, peer):
   if torch.cuda.device_count() < 2:
     pytest.skip("needs two GPUs")
   from colabfold_kernels import evoformer
-  world, port = 2, 29711 + os.getpid() % 200
-  mp.spawn(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+  world, port = 2, 29711 + os.getpid() % 200 + (300 if peer else 0)
+  mp.spawn(_worker, args=(world, port, str(tmp_path), peer), nprocs=world, join=True)
   msa, pair, msa_mask, pair_mask = _inputs()
   params = evoformer.init_params(seed=1, device="cuda")
   ref_m, ref_p = evoformer.block(evoformer.cuda_kernels(), msa.cuda(), pair.cuda(), msa_mask.cuda(), pair_mask.cuda(), params)
