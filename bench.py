@@ -122,7 +122,25 @@ def cpu_arm(steps, warmup, sample_b=32):
           "ms_per_sample": sec * 1e3, "steps_timed": n_timed, "warmup_run": n_warm, "sample_b": sample_b}
 
 
-def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False, fp8_attention=False, graph=True):
+_PEER = {}
+
+
+def peer_exchange(dev, want=True):
+  """One PeerExchange per process (the all-to-alls of the sharded block as the library's kernels over NVLink peer
+  memory), or None with the reason when symmetric memory cannot be set up: the block then uses NCCL's all-to-all."""
+  if not want:
+    return None, "nccl all_to_all_single (peer exchange switched off)"
+  if "x" not in _PEER:
+    from colabfold_kernels import evoformer
+    try:
+      _PEER["x"], _PEER["how"] = evoformer.PeerExchange(None, dev), "cfk_peer_alltoall over NVLink peer memory"
+    except Exception as e:  # no symmetric memory on this box / build
+      _PEER["x"], _PEER["how"] = None, f"nccl all_to_all_single (peer exchange unavailable: {type(e).__name__}: {str(e)[:120]})"
+  return _PEER["x"], _PEER["how"]
+
+
+def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_trimul=False, fp8_attention=False, graph=True,
+                       peer=True):
   """Second metric: one Evoformer block (inference wiring of the fused ops) at N_seq=512, N_res=1024, device-timed,
   max over ranks.  One GPU: the whole block; N GPUs: the same block row-sharded (total work fixed).  fp8_trimul: the
   reference's opt-in e4m3 contractions (triangle multiplication: half the bytes of the operand the ranks exchange; and
@@ -139,7 +157,8 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   params = evoformer.init_params(device=dev)
   K = evoformer.cuda_kernels()
   if world > 1:
-    blk = evoformer.ShardedBlock(K, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention, fp8_opm=fp8_trimul)
+    blk = evoformer.ShardedBlock(K, params, fp8_trimul=fp8_trimul, fp8_attention=fp8_attention, fp8_opm=fp8_trimul,
+                                 peer_exchange=peer_exchange(dev, peer)[0])
     msa_l, pair_l = msa[blk.shard(n_seq)].to(dev), pair[blk.shard(n_res)].to(dev)
     run = lambda: blk(msa_l, pair_l, msa_mask, pair_mask)
   else:
@@ -172,7 +191,7 @@ def evoformer_block_ms(world, rank, dev, iters=3, n_seq=512, n_res=1024, fp8_tri
   return float(ms), launch
 
 
-def block_matches_single_gpu(world, rank, dev, n_seq=64, n_res=256):
+def block_matches_single_gpu(world, rank, dev, n_seq=64, n_res=256, peer=True):
   """The row-sharded block against the one-GPU block on the same inputs at a small size: every rank runs its shard,
   rank 0 also runs the whole block and compares (max-abs error over max-abs value, both representations)."""
   import torch
@@ -186,7 +205,8 @@ def block_matches_single_gpu(world, rank, dev, n_seq=64, n_res=256):
   pair_mask = (torch.rand(n_res, n_res, generator=g) < 0.95).float().to(dev)
   params = evoformer.init_params(device=dev)
   K = evoformer.cuda_kernels()
-  blk = evoformer.ShardedBlock(K, params, exchange_triangle=True)  # the form the large ranks counts take
+  blk = evoformer.ShardedBlock(K, params, exchange_triangle=True,  # the form the large ranks counts take
+                               peer_exchange=peer_exchange(dev, peer)[0])
   m_l, p_l = blk(msa[blk.shard(n_seq)].contiguous(), pair[blk.shard(n_res)].contiguous(), msa_mask, pair_mask)
   m_all = torch.empty((world,) + tuple(m_l.shape), dtype=bf, device=dev)
   p_all = torch.empty((world,) + tuple(p_l.shape), dtype=bf, device=dev)
@@ -209,6 +229,8 @@ def main():
   ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
   ap.add_argument("--block", type=int, default=1, help="also time one Evoformer block (0 to skip)")
   ap.add_argument("--block-graph", type=int, default=1, help="replay the block as one CUDA graph (0: launch op by op)")
+  ap.add_argument("--peer-exchange", type=int, default=1,
+                  help="sharded block: all-to-alls as the library's kernels over NVLink peer memory (0: NCCL)")
   ap.add_argument("--e2e-chunks", type=int, default=8, help="pieces the batch is streamed in by the end-to-end step")
   ap.add_argument("--batch", type=int, default=B, help="batch rows per GPU (smaller values are for profiler captures only)")
   args = ap.parse_args()
@@ -369,17 +391,21 @@ def main():
   del ref_out, ref_lse, ref_dk
   if world > 1:
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-  block_ms = block_f8_ms = block_f8a_ms = block_launch = block_1gpu_ms = block_err = None
+  block_ms = block_f8_ms = block_f8a_ms = block_launch = block_1gpu_ms = block_err = block_nccl_ms = block_exchange = None
   if args.block:
     graph = args.block_graph != 0
+    peer = args.peer_exchange != 0
     if world > 1:
-      block_err = block_matches_single_gpu(world, rank, dev)
+      block_exchange = peer_exchange(dev, peer)[1]
+      block_err = block_matches_single_gpu(world, rank, dev, peer=peer)
       if rank == 0:  # the same block on this GPU alone: the denominator of the strong-scaling figure
         block_1gpu_ms, _ = evoformer_block_ms(1, 0, dev, graph=graph)
       dist.barrier()
-    block_ms, block_launch = evoformer_block_ms(world, rank, dev, graph=graph)
-    block_f8_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, graph=graph)
-    block_f8a_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, fp8_attention=True, graph=graph)
+    block_ms, block_launch = evoformer_block_ms(world, rank, dev, graph=graph, peer=peer)
+    if world > 1 and peer and peer_exchange(dev)[0] is not None:  # the same block with NCCL's all-to-all, for comparison
+      block_nccl_ms, _ = evoformer_block_ms(world, rank, dev, graph=graph, peer=False)
+    block_f8_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, graph=graph, peer=peer)
+    block_f8a_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, fp8_attention=True, graph=graph, peer=peer)
   status = ops.device_status()
   if rank == 0:
     sampler.stop_flag.set()
@@ -413,7 +439,8 @@ def main():
                    "evoformer_block": None if block_ms is None else {
                        "ms": block_ms, "ms_e4m3_contractions": block_f8_ms, "ms_e4m3_contractions_and_attention": block_f8a_ms, "launch": block_launch, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
-                       "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling, NCCL all-to-all / all-gather)"}},
+                       "ms_nccl_all_to_all": block_nccl_ms, "all_to_all": block_exchange,
+                       "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling; all-gathers by NCCL)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms), "chunks": n_chunks,
                 "matches_resident_step": e2e_ok},

@@ -174,25 +174,28 @@ class PeerExchange:
     self._handles = [symm.rendezvous(self.flags, self.group)]
     self.flag_ptrs = torch.tensor([int(p) for p in self._handles[0].buffer_ptrs], dtype=torch.int64, device=device)
     self.counter = torch.zeros(1, dtype=torch.int32, device=device)
-    self.sites = {}
+    self.sites, self._retired = {}, []
     dist.barrier(group)  # every rank's flags are zero before any peer counts on them
 
   def _site(self, site, nbytes):
     if site not in self.sites or self.sites[site][0].numel() < nbytes:
+      if site in self.sites:
+        self._retired.append(self.sites[site])  # a recorded graph may still write there: never handed back
       buf = self.symm.empty(nbytes, dtype=torch.uint8, device=self.device)
       h = self.symm.rendezvous(buf, self.group)
       self._handles.append(h)
       self.sites[site] = (buf, torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=self.device))
     return self.sites[site]
 
-  def all_to_all(self, site, x):
+  def all_to_all(self, site, x, out_shape=None, **strides):
     """x [P, ...] contiguous: part p goes to rank p -> [P, ...] with part q what rank q sent here (a view of the site's
-    receive buffer)."""
+    receive buffer).  With strides (ops.peer_alltoall) x is any contiguous tensor whose parts are strided runs, and
+    out_shape the shape of what arrives."""
     from colabfold_kernels import ops
     nbytes = x.numel() * x.element_size()
     buf, ptrs = self._site(site, nbytes)
-    ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, self.P)
-    return buf[:nbytes].view(x.dtype).view(x.shape)
+    ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, self.P, **strides)
+    return buf[:nbytes].view(x.dtype).view(x.shape if out_shape is None else out_shape)
 
 
 class ShardedBlock:
@@ -230,6 +233,12 @@ class ShardedBlock:
   def rows_to_cols(self, x):
     P = self.P
     n0, n1, c = x.shape
+    if self.peer is not None and (n1 // P * c * x.element_size()) % 16 == 0:
+      # part p = columns [p n1/P, (p+1) n1/P) of every local row, read in place; it lands as rows [rank n0, (rank+1) n0)
+      self._site_no += 1
+      run = n1 // P * c * x.element_size()
+      return self.peer.all_to_all(self._site_no, x.contiguous(), (P * n0, n1 // P, c), rows=n0, run_bytes=run, src_part=run,
+                                  src_row=P * run, dst_part=n0 * run, dst_row=run)
     send = x.reshape(n0, P, n1 // P, c).permute(1, 0, 2, 3).contiguous()
     return self._all_to_all(send).reshape(P * n0, n1 // P, c)
 
@@ -237,6 +246,12 @@ class ShardedBlock:
   def cols_to_rows(self, x):
     P = self.P
     n0, n1, c = x.shape
+    if self.peer is not None and (n1 * c * x.element_size()) % 16 == 0:
+      # part p = rows [p n0/P, (p+1) n0/P), contiguous; it lands as columns [rank n1, (rank+1) n1) of the receiver's rows
+      self._site_no += 1
+      run = n1 * c * x.element_size()
+      return self.peer.all_to_all(self._site_no, x.contiguous(), (n0 // P, P * n1, c), rows=n0 // P, run_bytes=run,
+                                  src_part=n0 // P * run, src_row=run, dst_part=run, dst_row=P * run)
     send = x.reshape(P, n0 // P, n1, c).contiguous()
     return self._all_to_all(send).permute(1, 0, 2, 3).reshape(n0 // P, P * n1, c)
 

@@ -158,13 +158,18 @@ def _packed_attention_qk8(p, p8, bias, kmask, gate_bias, column, trim, want_lse)
 
 
 # ------------------------------------------------------------------------------------------ peer all-to-all
-def peer_alltoall(send, recv_ptrs, flag_ptrs, counter, rank, parts):
-  """Part p of send [parts, ...] into rank p's receive buffer (device pointers in recv_ptrs), then the flag barrier."""
+def peer_alltoall(send, recv_ptrs, flag_ptrs, counter, rank, parts, rows=1, run_bytes=None, src_part=None, src_row=0,
+                  dst_part=None, dst_row=0):
+  """Part p of send into rank p's receive buffer (device pointers in recv_ptrs), then the flag barrier.  By default
+  send is [parts, chunk]; with rows / run_bytes / strides (bytes) a part is `rows` strided runs on either side."""
   send = _c(send)
   chunk = send.numel() * send.element_size() // parts
+  run_bytes = chunk if run_bytes is None else run_bytes
+  src_part = chunk if src_part is None else src_part
+  dst_part = chunk if dst_part is None else dst_part
   with torch.cuda.device(send.device):
-    _lib.call("cfk_peer_alltoall", _ptr(send), _ptr(recv_ptrs), _ptr(flag_ptrs), _ptr(counter), int(rank), int(parts), chunk,
-              _stream())
+    _lib.call("cfk_peer_alltoall", _ptr(send), _ptr(recv_ptrs), _ptr(flag_ptrs), _ptr(counter), int(rank), int(parts), int(rows),
+              int(run_bytes), int(src_part), int(src_row), int(dst_part), int(dst_row), _stream())
 
 
 # ------------------------------------------------------------------------------------------ contraction

@@ -10,25 +10,34 @@
 namespace cfk {
 namespace {
 
-// part p of `send` ([parts][chunk] bytes) goes to rank p, where it lands as part `rank` of that rank's receive buffer
+// Part p of the send buffer goes to rank p.  A part is `rows` runs of `run16` 16-byte pieces: run i of part p starts
+// src_part * p + src_row * i pieces into the send buffer and lands dst_part * rank + dst_row * i pieces into rank p's
+// receive buffer, so that a switch between row and column sharding needs no packing copy before and no re-layout copy
+// after the exchange (a plain [parts][chunk] all-to-all is rows = 1).
+struct PeerCopy {
+  int64_t rows, run16, src_part, src_row, dst_part, dst_row;
+};
+
 __global__ void __launch_bounds__(256) peer_alltoall_kernel(const uint4* __restrict__ send, void* const* __restrict__ recv_ptrs,
-                                                            int rank, int parts, int64_t chunk16, int blocks_per_part) {
+                                                            int rank, int parts, PeerCopy c, int blocks_per_part) {
   const int p = blockIdx.x / blocks_per_part, b = blockIdx.x % blocks_per_part;
   // start with the next rank so that the ranks do not all write to the same peer at the same time
   const int peer = (rank + 1 + p) % parts;
-  const uint4* src = send + int64_t(peer) * chunk16;
-  uint4* dst = static_cast<uint4*>(recv_ptrs[peer]) + int64_t(rank) * chunk16;
-  const int64_t stride = int64_t(blocks_per_part) * blockDim.x;
+  const uint4* src = send + int64_t(peer) * c.src_part;
+  uint4* dst = static_cast<uint4*>(recv_ptrs[peer]) + int64_t(rank) * c.dst_part;
+  const int64_t total = c.rows * c.run16, stride = int64_t(blocks_per_part) * blockDim.x;
+  auto so = [&](int64_t i) { const int64_t r = i / c.run16; return r * c.src_row + (i - r * c.run16); };
+  auto dof = [&](int64_t i) { const int64_t r = i / c.run16; return r * c.dst_row + (i - r * c.run16); };
   int64_t i = int64_t(b) * blockDim.x + threadIdx.x;
   // four independent 16-byte transfers in flight per thread
-  for (; i + 3 * stride < chunk16; i += 4 * stride) {
-    const uint4 v0 = src[i], v1 = src[i + stride], v2 = src[i + 2 * stride], v3 = src[i + 3 * stride];
-    dst[i] = v0;
-    dst[i + stride] = v1;
-    dst[i + 2 * stride] = v2;
-    dst[i + 3 * stride] = v3;
+  for (; i + 3 * stride < total; i += 4 * stride) {
+    const uint4 v0 = src[so(i)], v1 = src[so(i + stride)], v2 = src[so(i + 2 * stride)], v3 = src[so(i + 3 * stride)];
+    dst[dof(i)] = v0;
+    dst[dof(i + stride)] = v1;
+    dst[dof(i + 2 * stride)] = v2;
+    dst[dof(i + 3 * stride)] = v3;
   }
-  for (; i < chunk16; i += stride) dst[i] = src[i];
+  for (; i < total; i += stride) dst[dof(i)] = src[so(i)];
 }
 
 // Every rank tells every other that all it sent before this point has been written, then waits for the same from all.
@@ -66,23 +75,25 @@ __global__ void peer_barrier_kernel(int* const* __restrict__ flag_ptrs, int* __r
 using namespace cfk;
 
 extern "C" int cfk_peer_alltoall(const void* send, const void* recv_ptrs, const void* flag_ptrs, void* counter, int rank,
-                                 int parts, int64_t chunk_bytes, void* stream) {
+                                 int parts, int64_t rows, int64_t run_bytes, int64_t src_part_bytes, int64_t src_row_bytes,
+                                 int64_t dst_part_bytes, int64_t dst_row_bytes, void* stream) {
   if (!send || !recv_ptrs || !flag_ptrs || !counter) return CFK_ERR_NULL;
-  if (parts < 1 || parts > 32 || rank < 0 || rank >= parts || chunk_bytes < 0) return CFK_ERR_SHAPE;
-  if (chunk_bytes % 16 != 0 || !aligned16(send)) return CFK_ERR_ALIGN;
+  if (parts < 1 || parts > 32 || rank < 0 || rank >= parts || rows < 0 || run_bytes < 0) return CFK_ERR_SHAPE;
+  if ((run_bytes | src_part_bytes | src_row_bytes | dst_part_bytes | dst_row_bytes) % 16 != 0 || !aligned16(send)) return CFK_ERR_ALIGN;
   int* status = device_status_word();
   if (status == nullptr) return CFK_ERR_LAUNCH;
   auto st = static_cast<cudaStream_t>(stream);
-  if (chunk_bytes > 0) {
+  const PeerCopy c{rows, run_bytes / 16, src_part_bytes / 16, src_row_bytes / 16, dst_part_bytes / 16, dst_row_bytes / 16};
+  const int64_t total = c.rows * c.run16;
+  if (total > 0) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int bpp = (2 * sms + parts - 1) / parts;   // about two blocks per SM in all
-    const int64_t chunk16 = chunk_bytes / 16;
-    if (int64_t(bpp) * 256 > chunk16) bpp = int((chunk16 + 255) / 256);
+    if (int64_t(bpp) * 256 > total) bpp = int((total + 255) / 256);
     if (bpp < 1) bpp = 1;
     peer_alltoall_kernel<<<bpp * parts, 256, 0, st>>>(static_cast<const uint4*>(send), static_cast<void* const*>(recv_ptrs), rank,
-                                                      parts, chunk16, bpp);
+                                                      parts, c, bpp);
     int rc = check_launch();
     if (rc != CFK_OK) return rc;
   }

@@ -168,17 +168,20 @@ CFK_API int cfk_contract_gathered(const void* a, const void* b, void* out, int c
 CFK_API int cfk_contract_exchanged(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
                                    float alpha, int parts, int split_k, void* stream);
 
-/* All-to-all over NVLink peer memory for the row-sharded block (one process per GPU): part p of `send`
- * ([parts][chunk_bytes]) is written into rank p's receive buffer as its part `rank`, by plain 16-byte stores of a kernel
- * of this library (no TMA, no multicast), followed by a flag barrier after which every rank's receive buffer holds all
- * parts.  recv_ptrs: device array of `parts` pointers, entry p = rank p's receive buffer; flag_ptrs: device array of
- * `parts` pointers, entry p = rank p's array of `parts` int32 flags (zero-initialised); counter: one int32 on this device
- * (zero-initialised) that numbers the barriers, so that a replayed CUDA graph keeps counting.  Buffers and flags are
- * symmetric memory the caller set up (peer access enabled); chunk_bytes a multiple of 16.  The wait for the peers is
- * bounded (about a second): a missing peer leaves code 1901 in the device status word instead of a hang.  The
- * reference has no multi-GPU code; this replaces an NCCL all-to-all between kernels. */
+/* All-to-all over NVLink peer memory for the row-sharded block (one process per GPU): part p of `send` is written into
+ * rank p's receive buffer by plain 16-byte stores of a kernel of this library (no TMA, no multicast), followed by a flag
+ * barrier after which every rank's receive buffer holds all parts.  A part is `rows` runs of run_bytes: run i of part p
+ * is read at src_part_bytes * p + src_row_bytes * i and written at dst_part_bytes * rank + dst_row_bytes * i of rank p's
+ * buffer, so a switch between row and column sharding needs no packing or re-layout copy (rows = 1 is the plain
+ * [parts][chunk] exchange); all byte counts multiples of 16.  recv_ptrs: device array of `parts` pointers, entry p =
+ * rank p's receive buffer; flag_ptrs: device array of `parts` pointers, entry p = rank p's array of `parts` int32 flags
+ * (zero-initialised); counter: one int32 on this device (zero-initialised) that numbers the barriers, so that a replayed
+ * CUDA graph keeps counting.  Buffers and flags are symmetric memory the caller set up (peer access enabled).  The
+ * wait for the peers is bounded (about a second): a missing peer leaves code 1901 in the device status word instead of
+ * a hang.  The reference has no multi-GPU code; this replaces an NCCL all-to-all between kernels. */
 CFK_API int cfk_peer_alltoall(const void* send, const void* recv_ptrs, const void* flag_ptrs, void* counter, int rank,
-                              int parts, int64_t chunk_bytes, void* stream);
+                              int parts, int64_t rows, int64_t run_bytes, int64_t src_part_bytes, int64_t src_row_bytes,
+                              int64_t dst_part_bytes, int64_t dst_row_bytes, void* stream);
 
 /* The outer product of the outer-product-mean over the MSA depth, for 32-channel projections:
  * out[i, j, c, e] = sum_s a[i*32 + c, s] * b[j*32 + e, s]; a [ri*32, s], b [rj*32, s] in `dtype` (CFK_BF16 or CFK_E4M3),
