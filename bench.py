@@ -129,13 +129,13 @@ def peer_exchange(dev, want=True):
   """One PeerExchange per process (the all-to-alls of the sharded block as the library's kernels over NVLink peer
   memory), or None with the reason when symmetric memory cannot be set up: the block then uses NCCL's all-to-all."""
   if not want:
-    return None, "nccl all_to_all_single (peer exchange switched off)"
+    return None, "nccl all_to_all_single / all_gather (peer exchange switched off)"
   if "x" not in _PEER:
     from colabfold_kernels import evoformer
     try:
-      _PEER["x"], _PEER["how"] = evoformer.PeerExchange(None, dev), "cfk_peer_alltoall over NVLink peer memory"
+      _PEER["x"], _PEER["how"] = evoformer.PeerExchange(None, dev), "cfk_peer_alltoall: all-to-alls and all-gathers as stores into NVLink peer memory"
     except Exception as e:  # no symmetric memory on this box / build
-      _PEER["x"], _PEER["how"] = None, f"nccl all_to_all_single (peer exchange unavailable: {type(e).__name__}: {str(e)[:120]})"
+      _PEER["x"], _PEER["how"] = None, f"nccl all_to_all_single / all_gather (peer exchange unavailable: {type(e).__name__}: {str(e)[:120]})"
   return _PEER["x"], _PEER["how"]
 
 
@@ -402,7 +402,7 @@ def main():
         block_1gpu_ms, _ = evoformer_block_ms(1, 0, dev, graph=graph)
       dist.barrier()
     block_ms, block_launch = evoformer_block_ms(world, rank, dev, graph=graph, peer=peer)
-    if world > 1 and peer and peer_exchange(dev)[0] is not None:  # the same block with NCCL's all-to-all, for comparison
+    if world > 1 and peer and peer_exchange(dev)[0] is not None:  # the same block with NCCL's collectives, for comparison
       block_nccl_ms, _ = evoformer_block_ms(world, rank, dev, graph=graph, peer=False)
     block_f8_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, graph=graph, peer=peer)
     block_f8a_ms, _ = evoformer_block_ms(world, rank, dev, fp8_trimul=True, fp8_attention=True, graph=graph, peer=peer)
@@ -439,8 +439,8 @@ def main():
                    "evoformer_block": None if block_ms is None else {
                        "ms": block_ms, "ms_e4m3_contractions": block_f8_ms, "ms_e4m3_contractions_and_attention": block_f8a_ms, "launch": block_launch, "n_seq": 512, "n_res": 1024, "flop": 6.138e12,
                        "tflops": 6.138e12 / (block_ms * 1e-3) / 1e12,
-                       "ms_nccl_all_to_all": block_nccl_ms, "all_to_all": block_exchange,
-                       "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling; all-gathers by NCCL)"}},
+                       "ms_nccl_collectives": block_nccl_ms, "collectives": block_exchange,
+                       "mode": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (strong scaling)"}},
         "e2e": {"value": flops(B) * world / (float(e2e_ms) * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms), "chunks": n_chunks,
                 "matches_resident_step": e2e_ok},

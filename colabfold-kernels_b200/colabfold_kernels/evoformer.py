@@ -187,6 +187,23 @@ class PeerExchange:
       self.sites[site] = (buf, torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=self.device))
     return self.sites[site]
 
+  def all_gather(self, site, x, dim):
+    """Every rank's x concatenated along dim (0 or any later axis) -> a view of the site's receive buffer: each rank writes
+    its shard straight to where it belongs in every peer's result, so no concatenation copy follows."""
+    from colabfold_kernels import ops
+    x = x.contiguous()
+    es, P = x.element_size(), self.P
+    lead = 1
+    for d in x.shape[:dim]:
+      lead *= d
+    run = x.numel() // lead * es          # bytes of one leading-index slice of the local shard
+    buf, ptrs = self._site(site, P * x.numel() * es)
+    ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, P, rows=lead, run_bytes=run, src_part=0, src_row=run,
+                      dst_part=run, dst_row=P * run)
+    shape = list(x.shape)
+    shape[dim] *= P
+    return buf[:P * x.numel() * es].view(x.dtype).view(shape)
+
   def all_to_all(self, site, x, out_shape=None, **strides):
     """x [P, ...] contiguous: part p goes to rank p -> [P, ...] with part q what rank q sent here (a view of the site's
     receive buffer).  With strides (ops.peer_alltoall) x is any contiguous tensor whose parts are strided runs, and
@@ -257,6 +274,9 @@ class ShardedBlock:
 
   def gather(self, x, dim):
     x = x.contiguous()
+    if self.peer is not None and (x.numel() // max(1, math.prod(x.shape[:dim])) * x.element_size()) % 16 == 0:
+      self._site_no += 1
+      return self.peer.all_gather(self._site_no, x, dim)
     out = torch.empty((self.P * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     if x.element_size() == 1:  # e4m3 operands travel as bytes
       self.dist.all_gather_into_tensor(out.view(torch.uint8), x.view(torch.uint8), group=self.group)
