@@ -164,7 +164,10 @@ class PeerExchange:
   received stays valid until the same site runs again."""
 
   def __init__(self, group, device):
+    import os
     import torch.distributed as dist
+    # plain peer mappings are all this needs: no NVLink multicast object is bound to the buffers
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
     import torch.distributed._symmetric_memory as symm
     self.symm, self.group, self.device = symm, group if group is not None else dist.group.WORLD, device
     self.P, self.rank = dist.get_world_size(group), dist.get_rank(group)
