@@ -176,7 +176,7 @@ class PeerExchange:
     torch.cuda.synchronize(device)
     self._handles = [symm.rendezvous(self.flags, self.group)]
     self.flag_ptrs = torch.tensor([int(p) for p in self._handles[0].buffer_ptrs], dtype=torch.int64, device=device)
-    self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+    self.counter = torch.zeros(2, dtype=torch.int32, device=device)  # barrier number, finished blocks
     self.sites, self._retired = {}, []
     dist.barrier(group)  # every rank's flags are zero before any peer counts on them
 

@@ -10,6 +10,40 @@
 namespace cfk {
 namespace {
 
+// Every rank tells every other that all it sent before this point has been written, then waits for the same from all.
+// flags[r] is rank r's array of `parts` counters; counter[0] on this device numbers the barriers (it lives on the device
+// so that a replayed CUDA graph counts on).  One thread per peer; called by one whole block.
+__device__ void peer_barrier(int* const* __restrict__ flag_ptrs, int* __restrict__ counter, int rank, int parts, int* status,
+                             int code) {
+  __shared__ int s_epoch;
+  if (threadIdx.x == 0) s_epoch = *counter + 1;
+  __syncthreads();
+  const int epoch = s_epoch;
+  const int p = threadIdx.x;
+  if (p < parts) {
+    __threadfence_system();  // the data stores before this point are ordered before the flag
+    int* theirs = flag_ptrs[p] + rank;
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(theirs), "r"(epoch) : "memory");
+    const int* mine = flag_ptrs[rank] + p;
+    const long long t0 = clock64();
+    bool ok = false;
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (v - epoch >= 0) { ok = true; break; }
+      if (clock64() - t0 > (1ll << 31)) break;   // about a second: a peer is missing
+    }
+    if (!ok) report_timeout(status, code);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = epoch;
+}
+
+__global__ void peer_barrier_kernel(int* const* __restrict__ flag_ptrs, int* __restrict__ counter, int rank, int parts,
+                                    int* status, int code) {
+  peer_barrier(flag_ptrs, counter, rank, parts, status, code);
+}
+
 // Part p of the send buffer goes to rank p.  A part is `rows` runs of `run16` 16-byte pieces: run i of part p starts
 // src_part * p + src_row * i pieces into the send buffer and lands dst_part * rank + dst_row * i pieces into rank p's
 // receive buffer, so that a switch between row and column sharding needs no packing copy before and no re-layout copy
@@ -19,7 +53,9 @@ struct PeerCopy {
 };
 
 __global__ void __launch_bounds__(256) peer_alltoall_kernel(const uint4* __restrict__ send, void* const* __restrict__ recv_ptrs,
-                                                            int rank, int parts, PeerCopy c, int blocks_per_part) {
+                                                            int rank, int parts, PeerCopy c, int blocks_per_part,
+                                                            int* const* __restrict__ flag_ptrs, int* __restrict__ counter,
+                                                            int* status, int code) {
   const int p = blockIdx.x / blocks_per_part, b = blockIdx.x % blocks_per_part;
   // start with the next rank so that the ranks do not all write to the same peer at the same time
   const int peer = (rank + 1 + p) % parts;
@@ -38,35 +74,17 @@ __global__ void __launch_bounds__(256) peer_alltoall_kernel(const uint4* __restr
     dst[dof(i + 3 * stride)] = v3;
   }
   for (; i < total; i += stride) dst[dof(i)] = src[so(i)];
-}
-
-// Every rank tells every other that all it sent before this point has been written, then waits for the same from all.
-// flags[r] is rank r's array of `parts` counters; counter[0] on this device numbers the barriers (it lives on the device
-// so that a replayed CUDA graph counts on).  One thread per peer.
-__global__ void peer_barrier_kernel(int* const* __restrict__ flag_ptrs, int* __restrict__ counter, int rank, int parts,
-                                    int* status, int code) {
-  __shared__ int s_epoch;
-  if (threadIdx.x == 0) s_epoch = *counter + 1;
+  // the block that finishes last runs the barrier (counter[1] counts the finished blocks): no second launch
+  __shared__ int s_last;
+  __threadfence_system();
   __syncthreads();
-  const int epoch = s_epoch;
-  const int p = threadIdx.x;
-  if (p < parts) {
-    __threadfence_system();  // the data stores of the kernels before this one are ordered before the flag
-    int* theirs = flag_ptrs[p] + rank;
-    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(theirs), "r"(epoch) : "memory");
-    const int* mine = flag_ptrs[rank] + p;
-    const long long t0 = clock64();
-    bool ok = false;
-    while (true) {
-      int v;
-      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-      if (v - epoch >= 0) { ok = true; break; }
-      if (clock64() - t0 > (1ll << 31)) break;   // about a second: a peer is missing
-    }
-    if (!ok) report_timeout(status, code);
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(counter + 1, 1);
+    s_last = done == int(gridDim.x) - 1;
+    if (s_last) counter[1] = 0;
   }
   __syncthreads();
-  if (threadIdx.x == 0) *counter = epoch;
+  if (s_last) peer_barrier(flag_ptrs, counter, rank, parts, status, code);
 }
 
 }  // namespace
@@ -93,9 +111,9 @@ extern "C" int cfk_peer_alltoall(const void* send, const void* recv_ptrs, const 
     if (int64_t(bpp) * 256 > total) bpp = int((total + 255) / 256);
     if (bpp < 1) bpp = 1;
     peer_alltoall_kernel<<<bpp * parts, 256, 0, st>>>(static_cast<const uint4*>(send), static_cast<void* const*>(recv_ptrs), rank,
-                                                      parts, c, bpp);
-    int rc = check_launch();
-    if (rc != CFK_OK) return rc;
+                                                      parts, c, bpp, static_cast<int* const*>(flag_ptrs),
+                                                      static_cast<int*>(counter), status, 1901);
+    return check_launch();
   }
   peer_barrier_kernel<<<1, 32, 0, st>>>(static_cast<int* const*>(flag_ptrs), static_cast<int*>(counter), rank, parts, status, 1901);
   return check_launch();

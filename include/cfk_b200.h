@@ -175,8 +175,8 @@ CFK_API int cfk_contract_exchanged(const void* a, const void* b, void* out, int 
  * buffer, so a switch between row and column sharding needs no packing or re-layout copy (rows = 1 is the plain
  * [parts][chunk] exchange); all byte counts multiples of 16.  recv_ptrs: device array of `parts` pointers, entry p =
  * rank p's receive buffer; flag_ptrs: device array of `parts` pointers, entry p = rank p's array of `parts` int32 flags
- * (zero-initialised); counter: one int32 on this device (zero-initialised) that numbers the barriers, so that a replayed
- * CUDA graph keeps counting.  Buffers and flags are symmetric memory the caller set up (peer access enabled).  The
+ * (zero-initialised); counter: two int32 on this device (zero-initialised): the barrier number, so that a replayed CUDA
+ * graph keeps counting, and the count of finished blocks (the last block of the copy kernel runs the barrier).  Buffers and flags are symmetric memory the caller set up (peer access enabled).  The
  * wait for the peers is bounded (about a second): a missing peer leaves code 1901 in the device status word instead of
  * a hang.  The reference has no multi-GPU code; this replaces an NCCL all-to-all between kernels. */
 CFK_API int cfk_peer_alltoall(const void* send, const void* recv_ptrs, const void* flag_ptrs, void* counter, int rank,
