@@ -461,6 +461,24 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       }
     }
     // ---------------------------------------------------------------- epilogue: O / l, gate, store
+    // the gate rows of this group's batch rows are fetched before the wait for the last P V, so that their latency
+    // runs under it instead of after it
+    constexpr int kMine = (C::G + 1) / 2;   // batch rows of one group: grp, grp + 2, ...
+    uint4 gpre[kMine][D / 8];
+    {
+      const int q = q0 + row;
+#pragma unroll
+      for (int k = 0; k < kMine; ++k) {
+        const int g = grp + 2 * k;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) gpre[k][c] = make_uint4(0, 0, 0, 0);
+        if (ok && p.gate != nullptr && g < gcount && q < p.sq) {
+          const __nv_bfloat16* gate = static_cast<const __nv_bfloat16*>(p.gate) + (b0 + g) * p.sg_.b + head * p.sg_.h + int64_t(q) * p.sg_.s;
+#pragma unroll
+          for (int c = 0; c < D / 8; ++c) gpre[k][c] = *reinterpret_cast<const uint4*>(gate + c * 8);
+        }
+      }
+    }
     if (uses > 0) {
       CFK_SOFTMAX_WAIT(&pv_done[grp], (uses - 1) & 1, 304)
       tc_fence_after();
@@ -468,8 +486,10 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 #undef CFK_SOFTMAX_WAIT
     if (ok) {
       const int q = q0 + row;
-#pragma unroll 1
-      for (int g = grp; g < gcount; g += 2) {
+#pragma unroll
+      for (int k = 0; k < kMine; ++k) {
+        const int g = grp + 2 * k;
+        if (g >= gcount) break;
         const int b = b0 + g;
         const float m_ref = st_m[g * 128], l_run = st_l[g * 128];
         float o[D];
@@ -480,9 +500,6 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           bool zero_row = false;
           if (p.trim != nullptr) zero_row = p.trim[b] == 0 || q >= p.trim[p.nb];
           const float inv = zero_row ? 0.f : 1.0f / l_run;
-          const __nv_bfloat16* gate =
-              p.gate == nullptr ? nullptr
-                                : static_cast<const __nv_bfloat16*>(p.gate) + b * p.sg_.b + head * p.sg_.h + int64_t(q) * p.sg_.s;
           const __nv_bfloat16* gb =
               p.gate == nullptr ? nullptr : static_cast<const __nv_bfloat16*>(p.gate_bias) + int64_t(head) * D;
           __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + b * p.so_.b + head * p.so_.h + int64_t(q) * p.so_.s;
@@ -491,8 +508,8 @@ attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             float v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = o[c * 8 + i] * inv;
-            if (gate != nullptr) {
-              const uint4 gw = *reinterpret_cast<const uint4*>(gate + c * 8);
+            if (p.gate != nullptr) {
+              const uint4 gw = gpre[k][c];
               const uint4 bw = *reinterpret_cast<const uint4*>(gb + c * 8);
               const uint32_t gg[4] = {gw.x, gw.y, gw.z, gw.w}, bb[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
