@@ -263,9 +263,16 @@ opm_fused_kernel(const __grid_constant__ CUtensorMap tm_l, const __grid_constant
       const bool valid = gi < prm.ri && gj < prm.rj;
       const int64_t pair = int64_t(gi) * prm.rj + gj;
       const float inv = valid ? 1.0f / (prm.eps + __ldg(prm.norm + pair)) : 0.f;
+      // the residual row is fetched before the wait for the second GEMM, so that its latency runs under that wait
+      uint4 xpre[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        xpre[u] = make_uint4(0, 0, 0, 0);
+        if (valid && prm.residual != nullptr) xpre[u] = *reinterpret_cast<const uint4*>(prm.residual + pair * kF + g * 64 + u * 8);
+      }
       CFK_OPM_WAIT(acc2_full, ti & 1, 1410)
       tc_fence_after();
-#pragma unroll 1
+#pragma unroll
       for (int cb = 0; cb < 2; ++cb) {
         uint32_t r[32];
         tmem_ld_x32(tmem + lane_addr + kColAcc2O + g * 64 + cb * 32, r);
@@ -281,8 +288,7 @@ opm_fused_kernel(const __grid_constant__ CUtensorMap tm_l, const __grid_constant
             const int col = g * 64 + cb * 32 + ch * 8;
             const uint4 bw = __ldg(reinterpret_cast<const uint4*>(prm.bias + col));
             const uint32_t bb[4] = {bw.x, bw.y, bw.z, bw.w};
-            uint4 xw = make_uint4(0, 0, 0, 0);
-            if (prm.residual != nullptr) xw = *reinterpret_cast<const uint4*>(prm.residual + pair * kF + col);
+            const uint4 xw = xpre[cb * 4 + ch];
             const uint32_t xx[4] = {xw.x, xw.y, xw.z, xw.w};
             uint32_t y[4];
 #pragma unroll
