@@ -166,6 +166,11 @@ extern "C" int cfk_ln_projection(const void* x, const float* ln_scale, const flo
                                      static_cast<cudaStream_t>(stream));
     if (rc != CFK_ERR_UNSUPPORTED) return rc;
   }
+  if (a == 128 && !f8) {  // the pair shape has a kernel of its own (weights resident, LayerNorm folded around the GEMM)
+    const int rc = ln_proj128_launch(x, ln_scale, ln_offset, w, keep, keep_dtype, p_out, m, g, n, eps,
+                                     static_cast<cudaStream_t>(stream));
+    if (rc != CFK_ERR_UNSUPPORTED) return rc;
+  }
   RowGemmParams prm{};
   prm.src[0] = row_major(x, a, ln_scale, ln_offset);
   prm.outer = 1; prm.inner = m; prm.inner_pad = m; prm.eps = eps;

@@ -82,6 +82,11 @@ int make_weight_map(CUtensorMap* m, const void* w, int slots, int k, int n);
 int ln_proj256_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* w, const void* keep,
                       int keep_dtype, void* out, int64_t m, int slots, int n, float eps, cudaStream_t st);
 
+// LayerNorm -> packed projection at 128 input channels and at most 512 output columns, weights resident and LayerNorm
+// folded around the GEMM (ln_proj128_sm100.cu); returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.
+int ln_proj128_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* w, const void* keep,
+                      int keep_dtype, void* out, int64_t m, int slots, int n, float eps, cudaStream_t st);
+
 // LayerNorm -> gated dual projection at 128 channels in and 128 + 128 out, channel-major bf16 (ln_gdp128_sm100.cu);
 // returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.
 int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* wp, const void* bp,

@@ -148,7 +148,7 @@ def test_ln_projection(m, a, g, n, h):
   chk(p, rp); chk(b, rb)
   p8, _ = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), None, f8=True, f8_scale=0.5)
   assert O.rms_err(p8.cpu().float(), rp * 0.5) <= 5e-2  # tests/test_ln_fusions.py:192
-  if a == 256:  # the 256-channel kernel's own row-block skipping: block 1 unkept (zeros), block 2 negative (unwritten)
+  if a in (128, 256):  # the shape kernels' own row-block skipping: block 1 unkept (zeros), block 2 negative (unwritten)
     keep = torch.ones(m)
     keep[128:256] = 0
     keep[256:384] = -1
@@ -157,6 +157,22 @@ def test_ln_projection(m, a, g, n, h):
     assert torch.equal(pk[live.cuda()], p[live.cuda()])
     assert m <= 128 or float(pk[128:256].float().abs().max()) == 0.0
     assert ops.device_status() == 0
+
+
+def test_ln_projection_rows_far_from_zero_mean():
+  """The 128-channel kernel multiplies the raw rows and takes the mean's part out afterwards (LN(x) w = rstd (x w' - mean s)
+  + t): rows whose mean is many standard deviations from zero must come out as the reference's normalise-then-multiply
+  (packed_attn.py:215-231)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(41)
+  m, a, g, n = 700, 128, 4, 128
+  x = (rnd(rng, m, a).float() + torch.linspace(-24, 24, m)[:, None]).to(torch.bfloat16)
+  w = rnd(rng, g, a, n, s=a ** -.5)
+  sc, of = 1 + rnd(rng, a, s=.1).float(), rnd(rng, a, s=.1).float()
+  p, _ = ops.ln_projection(x.cuda(), sc.cuda(), of.cuda(), w.cuda(), None)
+  assert ops.device_status() == 0
+  rp, _ = O.ref_ln_projection(x, sc, of, w, None)
+  chk(p, rp)
 
 
 @pytest.mark.parametrize("m,k,c", [(4101, 128, 128), (59, 64, 64), (1000, 256, 256), (1, 128, 256)])
