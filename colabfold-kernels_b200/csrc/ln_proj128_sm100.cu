@@ -4,21 +4,23 @@
 // All the weights (128 KB) stay in shared memory and LayerNorm is folded around the GEMM instead of being applied to the
 // tile: with w'[k][f] = scale[k] w[k][f] (rounded to bf16, prepared once per CTA in shared memory), s[f] = sum_k w'[k][f]
 // and t[f] = sum_k offset[k] w[k][f],
-//   LN(x) w = rstd * (x w' - mean * s) + t
-// so the MMAs run on the RAW tile as TMA lands it, two tiles are in flight, and nothing waits for a normalised tile.
-// Every worker thread owns one row in both roles (statistics of the row from the raw tile, then the row's part of every
-// accumulator), so the statistics never leave its registers.  s uses the same bf16 w' the tensor core multiplies by, so
-// mean * s cancels the mean's part of x w' to fp32 rounding.
+//   LN(x) w = rstd * (x w' - mean * s + std * t),   std = 1 / rstd
+// so the MMAs run on the RAW tile as TMA lands it and nothing waits for a normalised tile.  The rank-two correction
+// (- mean * s + std * t) is itself one more K step on the tensor core: the A operand gets a 16-wide extra tile whose row
+// holds -mean and std, the B operand 16 extra rows holding s and t, each fp32 value split into a bf16 head and a bf16
+// remainder with all four cross products present (head*head, head*rem, rem*head, rem*rem: relative error about 2^-17).
+// The epilogue is then one multiplication by rstd per element: no per-column constants are read, which matters because
+// a load of a constant that the 32 threads of a warp share still costs the shared-memory pipe as much as a full load,
+// and that pipe, not HBM, bounded the first form of this kernel.  s uses the same bf16 w' the tensor core multiplies
+// by, so mean * s cancels the mean's part of x w' to fp32 rounding.
 //
-// A persistent CTA walks 128-row tiles.  Warp 0: TMA producer (weights once, then two stages of activation tiles).
-// Warp 1: MMA issuer, 8 MMAs of M = 128, N = 256 (two 128-column chunks; N = 128 for an odd last chunk) into one of two
-// accumulators, so the activation tile is read from shared memory once per 256 output columns.  Warps 2-3: one store
-// thread per worker group (TMA store of the group's staging atom, then the hand-back once the store has read it), so
-// that neither the store's issue nor its read of the atom sits in the workers' path.  Warps 4-11: weight preparation,
-// statistics, and per chunk both groups of four warps drain the accumulator (group = 64-column half), apply the fold
-// and round to bf16 into their staging atom.  The column constants of a chunk live in the registers of 64 threads of
-// each group and are handed to the group through 512 bytes of shared memory per chunk (there is no room for all of
-// them beside the weights).  Row blocks follow `keep` (transition.py:29-38).  Every mbarrier wait is deadline-bounded.
+// A persistent CTA walks 128-row tiles.  Warp 0: TMA producer (weights once, then the activation tile).  Warp 1: MMA
+// issuer, per 256 output columns 8 MMAs of M = 128, N = 256 on the raw tile plus the correction step (N = 128 for an odd
+// last chunk) into one of two accumulators.  Warps 2-3: one store thread per worker group (TMA store of the group's
+// staging atom, then the hand-back once the store has read it).  Warps 4-11: weight preparation, the statistics of
+// the thread's own row (fp32 sum and sum of squares from the raw tile) and its correction entries, and per chunk both
+// groups of four warps drain the accumulator (group = 64-column half), scale by rstd and round to bf16 into their
+// staging atom.  Row blocks follow `keep` (transition.py:29-38).  Every mbarrier wait is deadline-bounded.
 #include "attention_sm100.cuh"
 #include "rowgemm_sm100.cuh"
 
@@ -33,11 +35,13 @@ constexpr int kThreads8 = 384;
 constexpr int kMaxTiles8 = 256;          // tiles per CTA when row blocks may be skipped
 constexpr int kAtom8 = 128 * 128;        // 16 KB: 128 lines of 128 bytes
 constexpr int kOffW8 = 0;                              // chunk c: atoms 2c, 2c + 1 ([128 k][64 columns])
-constexpr int kOffX8 = kOffW8 + 2 * kMaxChunks8 * kAtom8;   // two stages of 2 atoms ([128 rows][64 channels])
-constexpr int kOffO8 = kOffX8 + 4 * kAtom8;            // one staging atom per group ([128 rows][64 columns])
-constexpr int kOffCst8 = kOffO8 + 2 * kAtom8;          // per group: s[64] then t[64] of the chunk being drained
-constexpr int kOffBar8 = kOffCst8 + 2 * 128 * 4;
-constexpr int kNumBars8 = 2 + 2 + 2 + 2 + 2 + 2 + 2;
+constexpr int kWxAtom8 = 16 * 128;                     // correction rows of 64 columns: 16 lines of 128 bytes
+constexpr int kOffWx8 = kOffW8 + 2 * kMaxChunks8 * kAtom8;  // chunk c: atoms 2c, 2c + 1 ([16 k][64 columns])
+constexpr int kOffX8 = kOffWx8 + 2 * kMaxChunks8 * kWxAtom8;  // the activation tile: 2 atoms ([128 rows][64 channels])
+constexpr int kOffAx8 = kOffX8 + 2 * kAtom8;           // correction entries of the tile's rows: [128 rows][64 bytes]
+constexpr int kOffO8 = kOffAx8 + 128 * 64;             // one staging atom per group ([128 rows][64 columns])
+constexpr int kOffBar8 = kOffO8 + 2 * kAtom8;
+constexpr int kNumBars8 = 5 + 2 + 2 + 2 + 2;
 constexpr int kOffTmem8 = kOffBar8 + kNumBars8 * 8;
 constexpr int kOffCls8 = kOffTmem8 + 16;
 constexpr int kSmem8 = kOffCls8 + kMaxTiles8 + 1024;
@@ -69,9 +73,10 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar8);
   uint64_t* w_full = bars;            // the weights have landed
   uint64_t* w_ready = w_full + 1;     // ... and are scaled
-  uint64_t* x_full = w_ready + 1;     // [2] a tile has landed
-  uint64_t* x_free = x_full + 2;      // [2] its MMAs have completed and every worker warp has its statistics
-  uint64_t* acc_full = x_free + 2;    // [2]
+  uint64_t* x_full = w_ready + 1;     // the tile has landed
+  uint64_t* x_free = x_full + 1;      // its MMAs have completed and every worker warp has its statistics
+  uint64_t* ax_ready = x_free + 1;    // the correction entries of the tile's rows are written
+  uint64_t* acc_full = ax_ready + 1;  // [2]
   uint64_t* acc_empty = acc_full + 2; // [2]
   uint64_t* stg_full = acc_empty + 2; // [2] a group's staging atom is written
   uint64_t* stg_free = stg_full + 2;  // [2] ... and its store has read it
@@ -82,9 +87,10 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
   if (threadIdx.x == 0) {
     mbar_init(w_full, 1);
     mbar_init(w_ready, 8);
+    mbar_init(x_full, 1);
+    mbar_init(x_free, 9);
+    mbar_init(ax_ready, 4);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&x_full[i], 1);
-      mbar_init(&x_free[i], 9);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 8);
       mbar_init(&stg_full[i], 4);
@@ -142,12 +148,11 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       bool ok = true;
       uint32_t seq = 0, ti = 0;
       for (int64_t tile = next_computed(seq); tile >= 0 && ok; tile = next_computed(++seq), ++ti) {
-        const int st = ti & 1;
-        ok = mbar_wait_deadline(&x_free[st], ((ti >> 1) & 1) ^ 1);
+        ok = mbar_wait_deadline(x_free, (ti & 1) ^ 1);
         if (!ok) { report_timeout(prm.status, 1801); break; }
-        mbar_arrive_expect_tx(&x_full[st], 2 * kAtom8);
-        tma_load_2d(smem + kOffX8 + (2 * st) * kAtom8, &tm_x, &x_full[st], 0, int(tile * kRows8));
-        tma_load_2d(smem + kOffX8 + (2 * st + 1) * kAtom8, &tm_x, &x_full[st], 64, int(tile * kRows8));
+        mbar_arrive_expect_tx(x_full, 2 * kAtom8);
+        tma_load_2d(smem + kOffX8, &tm_x, x_full, 0, int(tile * kRows8));
+        tma_load_2d(smem + kOffX8 + kAtom8, &tm_x, x_full, 64, int(tile * kRows8));
       }
     }
     __syncwarp();
@@ -157,14 +162,14 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
       constexpr uint32_t idesc1 = make_idesc(kRows8, kNC8, 1, 1, 0, 1);       // A = raw x tile K-major, B = w' MN-major
       constexpr uint32_t idesc2 = make_idesc(kRows8, 2 * kNC8, 1, 1, 0, 1);   // two chunks at once
       constexpr uint32_t hi = desc_hi(1024, kSwz128);
+      constexpr uint32_t hi_ax = desc_hi(8 * 64, kSwz64);   // correction entries: 64-byte rows
+      const uint32_t x_k = desc_lo(smem_u32(smem + kOffX8), 16), ax_k = desc_lo(smem_u32(smem + kOffAx8), 16);
       bool ok = mbar_wait_deadline(w_ready, 0);
       if (!ok) report_timeout(prm.status, 1802);
       uint32_t seq = 0, ti = 0, cc = 0;
       for (int64_t tile = next_computed(seq); tile >= 0 && ok; tile = next_computed(++seq), ++ti) {
-        const int st = ti & 1;
-        ok = mbar_wait_deadline(&x_full[st], (ti >> 1) & 1);
+        ok = mbar_wait_deadline(x_full, ti & 1);
         if (!ok) { report_timeout(prm.status, 1803); break; }
-        const uint32_t x_k = desc_lo(smem_u32(smem + kOffX8 + (2 * st) * kAtom8), 16);
         for (int c = 0; c < prm.chunks && ok; c += 2, ++cc) {
           const int buf = cc & 1;
           ok = mbar_wait_deadline(&acc_empty[buf], ((cc >> 1) & 1) ^ 1);
@@ -175,9 +180,15 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
 #pragma unroll
           for (int kk = 0; kk < kK8 / 16; ++kk)
             mma_f16_ss2(tmem + buf * 2 * kNC8, x_k + (kk / 4) * (kAtom8 >> 4) + (kk % 4) * 2, hi, b + kk * 128, hi, idesc, kk > 0);
+          if (c == 0) {  // the correction step needs the rows' statistics; the steps above did not
+            ok = mbar_wait_deadline(ax_ready, ti & 1);
+            if (!ok) { report_timeout(prm.status, 1810); break; }
+            tc_fence_after();
+          }
+          mma_f16_ss2(tmem + buf * 2 * kNC8, ax_k, hi_ax, desc_lo(smem_u32(smem + kOffWx8 + (2 * c) * kWxAtom8), kWxAtom8), hi, idesc, 1);
           mma_commit(&acc_full[buf]);
         }
-        if (ok) mma_commit(&x_free[st]);
+        if (ok) mma_commit(x_free);
       }
     }
     __syncwarp();
@@ -208,17 +219,22 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const int pt = (warp - 4) * 32 + lane;
     uint8_t* stage = smem + kOffO8 + grp * kAtom8;
-    float* cst = reinterpret_cast<float*>(smem + kOffCst8) + grp * 128;
     bool ok = true;
 #define CFK_P8_WAIT(bar, parity, code)                            \
   if (ok && !mbar_wait_deadline((bar), (parity))) {               \
     report_timeout(prm.status, (code));                           \
     ok = false;                                                   \
   }
-    // ---- once: scale the weights' rows by the LayerNorm scales and take the column constants.  Thread (group, j, h)
-    // owns column grp * 64 + j of chunks 2h and 2h + 1 and keeps their constants.
+    // head and remainder of an fp32 value as two bf16
+    auto split = [](float v, __nv_bfloat16& hd, __nv_bfloat16& rm) {
+      hd = __float2bfloat16_rn(v);
+      rm = __float2bfloat16_rn(v - __bfloat162float(hd));
+    };
+    // ---- once: scale the weights' rows by the LayerNorm scales and write the correction rows.  Thread (group, j, h)
+    // owns column grp * 64 + j of chunks 2h and 2h + 1.  Correction rows: 0-3 = s head, s rem, s head, s rem;
+    // 4-7 = t head, t rem, t head, t rem; 8-15 = 0 (and the entries of a row: -mean head, head, rem, rem; std head,
+    // head, rem, rem; 0 ...), so that the K step adds (-mean) * s + std * t with every cross product.
     const int cj = trow & 63, chh = trow >> 6;
-    float cs[2] = {0.f, 0.f}, ct[2] = {0.f, 0.f};
     CFK_P8_WAIT(w_full, 0, 1805)
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -235,18 +251,24 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           s += __bfloat162float(ws);
           t = fmaf(__ldg(prm.ln_offset + k), w, t);
         }
-        cs[u] = s;
-        ct[u] = t;
+        __nv_bfloat16 sh, sr, th, tr;
+        split(s, sh, sr);
+        split(t, th, tr);
+        uint8_t* xb = smem + kOffWx8 + (2 * c + grp) * kWxAtom8;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const __nv_bfloat16 v = k >= 8 ? __float2bfloat16_rn(0.f) : (k < 4 ? ((k & 1) ? sr : sh) : ((k & 1) ? tr : th));
+          *reinterpret_cast<__nv_bfloat16*>(xb + k * 128 + (((cj >> 3) ^ (k & 7)) << 4) + (cj & 7) * 2) = v;
+        }
       }
+    }
+    if (grp == 0) {  // K = 8 .. 15 of the rows' correction entries stay zero
+      *reinterpret_cast<uint4*>(smem + kOffAx8 + swz_off(trow, 1, 64)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(smem + kOffAx8 + swz_off(trow, 0, 64)) = make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(w_ready);
-
-    if (chh == 0) {  // the constants of chunk 0 for the first tile; after that every chunk leaves the next one's
-      cst[cj] = cs[0];
-      cst[64 + cj] = ct[0];
-    }
 
     uint32_t seq = 0, ti = 0, cc = 0, sc = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++seq) {
@@ -260,12 +282,11 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         }
         continue;
       }
-      const int st = ti & 1;
       // ---- statistics of this thread's row from the raw tile (fp32 sum and sum of squares over the 128 channels)
-      CFK_P8_WAIT(&x_full[st], (ti >> 1) & 1, 1806)
-      float nmean, rstd;
+      CFK_P8_WAIT(x_full, ti & 1, 1806)
+      float rstd;
       {
-        const uint8_t* xt = smem + kOffX8 + (2 * st) * kAtom8;
+        const uint8_t* xt = smem + kOffX8;
         uint64_t s2a = f2_pack(0.f, 0.f), s2b = s2a, q2a = s2a, q2b = s2a;   // packed pairs, two chains
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
@@ -285,15 +306,25 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
         f2_unpack(f2_add(s2a, s2b), s0, s1);
         f2_unpack(f2_add(q2a, q2b), q0, q1);
         const float mean = (s0 + s1) * (1.0f / kK8);
-        const float var = fmaxf((q0 + q1) * (1.0f / kK8) - mean * mean, 0.f);
-        rstd = rsqrtf(var + prm.eps);
-        nmean = -mean;
+        const float var = fmaxf((q0 + q1) * (1.0f / kK8) - mean * mean, 0.f) + prm.eps;
+        rstd = rsqrtf(var);
+        if (grp == 0) {  // the row's correction entries (the other group computes the same numbers for its own epilogue)
+          __nv_bfloat16 mh, mr, dh, dr;
+          split(-mean, mh, mr);
+          split(var * rstd, dh, dr);
+          auto two = [](__nv_bfloat16 v) { return uint32_t(__bfloat16_as_ushort(v)) * 0x10001u; };
+          *reinterpret_cast<uint4*>(smem + kOffAx8 + swz_off(trow, 0, 64)) = make_uint4(two(mh), two(mr), two(dh), two(dr));
+          fence_proxy_async();
+        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&x_free[st]);
-      const uint64_t nm2 = f2_pack(nmean, nmean), r2 = f2_pack(rstd, rstd);
+      if (lane == 0) {
+        if (grp == 0) mbar_arrive(ax_ready);
+        mbar_arrive(x_free);
+      }
+      const uint64_t r2 = f2_pack(rstd, rstd);
 
-      // ---- per chunk: this group's 64 columns of the accumulator -> fold -> bf16 -> staging atom -> the store thread
+      // ---- per chunk: this group's 64 columns of the accumulator -> * rstd -> bf16 -> staging atom -> the store thread
 #pragma unroll 1
       for (int c = 0; c < prm.chunks; ++c, ++sc) {
         const int buf = cc & 1, hf = c & 1;
@@ -311,40 +342,19 @@ ln_proj128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constan
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
           ++cc;
         }
-        named_bar_sync(3 + grp, 128);  // this chunk's constants are in place
-        uint32_t y[32];
+        CFK_P8_WAIT(&stg_free[grp], (sc & 1) ^ 1, 1809)  // the store of the chunk before has read the staging atom
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const uint32_t* r = q < 4 ? r0 : r1;
           const int o = (q & 3) * 8;
-          const float4 sa = *reinterpret_cast<const float4*>(cst + q * 8), sb = *reinterpret_cast<const float4*>(cst + q * 8 + 4);
-          const float4 ta = *reinterpret_cast<const float4*>(cst + 64 + q * 8), tb = *reinterpret_cast<const float4*>(cst + 64 + q * 8 + 4);
-          const uint64_t y0 = f2_fma(f2_fma(nm2, f2_pack(sa.x, sa.y), f2_pack(__uint_as_float(r[o]), __uint_as_float(r[o + 1]))), r2, f2_pack(ta.x, ta.y));
-          const uint64_t y1 = f2_fma(f2_fma(nm2, f2_pack(sa.z, sa.w), f2_pack(__uint_as_float(r[o + 2]), __uint_as_float(r[o + 3]))), r2, f2_pack(ta.z, ta.w));
-          const uint64_t y2 = f2_fma(f2_fma(nm2, f2_pack(sb.x, sb.y), f2_pack(__uint_as_float(r[o + 4]), __uint_as_float(r[o + 5]))), r2, f2_pack(tb.x, tb.y));
-          const uint64_t y3 = f2_fma(f2_fma(nm2, f2_pack(sb.z, sb.w), f2_pack(__uint_as_float(r[o + 6]), __uint_as_float(r[o + 7]))), r2, f2_pack(tb.z, tb.w));
           float a0, a1, a2, a3, a4, a5, a6, a7;
-          f2_unpack(y0, a0, a1);
-          f2_unpack(y1, a2, a3);
-          f2_unpack(y2, a4, a5);
-          f2_unpack(y3, a6, a7);
-          y[q * 4 + 0] = pack_bf16x2(a0, a1);
-          y[q * 4 + 1] = pack_bf16x2(a2, a3);
-          y[q * 4 + 2] = pack_bf16x2(a4, a5);
-          y[q * 4 + 3] = pack_bf16x2(a6, a7);
+          f2_unpack(f2_mul(r2, f2_pack(__uint_as_float(r[o]), __uint_as_float(r[o + 1]))), a0, a1);
+          f2_unpack(f2_mul(r2, f2_pack(__uint_as_float(r[o + 2]), __uint_as_float(r[o + 3]))), a2, a3);
+          f2_unpack(f2_mul(r2, f2_pack(__uint_as_float(r[o + 4]), __uint_as_float(r[o + 5]))), a4, a5);
+          f2_unpack(f2_mul(r2, f2_pack(__uint_as_float(r[o + 6]), __uint_as_float(r[o + 7]))), a6, a7);
+          *reinterpret_cast<uint4*>(stage + swz_off(trow, q, 128)) =
+              make_uint4(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3), pack_bf16x2(a4, a5), pack_bf16x2(a6, a7));
         }
-        named_bar_sync(3 + grp, 128);  // every thread of the group has used the constants: the next chunk's go in
-        {
-          const int nx = c + 1 == prm.chunks ? 0 : c + 1;
-          if (chh == (nx >> 1)) {
-            cst[cj] = (nx & 1) ? cs[1] : cs[0];
-            cst[64 + cj] = (nx & 1) ? ct[1] : ct[0];
-          }
-        }
-        CFK_P8_WAIT(&stg_free[grp], (sc & 1) ^ 1, 1809)  // the store of the chunk before has read the staging atom
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          *reinterpret_cast<uint4*>(stage + swz_off(trow, q, 128)) = make_uint4(y[q * 4], y[q * 4 + 1], y[q * 4 + 2], y[q * 4 + 3]);
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&stg_full[grp]);
