@@ -86,6 +86,25 @@ def test_ln_gdp_pair(transpose, fp8):
   assert float(l.cpu().float()[..., inner:].abs().max()) == 0.0
 
 
+def test_ln_gdp_rows_far_from_zero_mean():
+  """The 128-channel kernel multiplies the raw rows and adds the LayerNorm correction (-mean s + std t) as one more K
+  step (split bf16 heads and remainders): rows whose mean is many standard deviations from zero must come out as the
+  reference's normalise-then-multiply (tri_mul.py:222-300)."""
+  from colabfold_kernels import ops
+  rng = np.random.default_rng(42)
+  a, b, k, p = 40, 200, 128, 256
+  x = (rnd(rng, a, b, k).float() + torch.linspace(-24, 24, a * b).reshape(a, b, 1)).to(bf)
+  wp, bp, wg, bg = rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1), rnd(rng, k, p, s=k ** -.5), rnd(rng, p, s=.1)
+  sc, of = 1 + rnd(rng, k, s=.1).float(), rnd(rng, k, s=.1).float()
+  mask = torch.ones(a, b, dtype=bf)
+  for transpose in (False, True):
+    l, r = ops.ln_gated_dual_proj(x.cuda(), sc.cuda(), of.cuda(), wp.cuda(), bp.cuda(), wg.cuda(), bg.cuda(), mask.cuda(),
+                                  transpose=transpose, pad=16)
+    assert ops.device_status() == 0
+    rl, rr = O.ref_ln_gdp(x, sc, of, wp, bp, wg, bg, mask, transpose=transpose, pad=16)
+    chk(l, rl); chk(r, rr)
+
+
 def test_ln_gdp_e4m3_per_tensor_scale():
   """A projection whose values sit below e4m3's normal range (weights scaled by 2^-7): unscaled, the cast flushes
   most of them (large error); with a per-tensor scale of 2^7 before rounding and alpha = 2^-14 on the contraction the
@@ -136,7 +155,8 @@ def test_trimul_epilogue(m, c, xdt):
 
 
 @pytest.mark.parametrize("m,a,g,n,h", [(4101, 128, 4, 128, 4), (59, 64, 4, 64, 4), (1000, 256, 4, 256, 8), (1, 128, 3, 128, 4),
-                                       (40000, 256, 4, 256, 8), (300, 256, 1, 128, 8), (777, 256, 3, 64, 4)])
+                                       (40000, 256, 4, 256, 8), (300, 256, 1, 128, 8), (777, 256, 3, 64, 4),
+                                       (30000, 128, 3, 128, 4), (257, 128, 2, 256, 4), (129, 128, 1, 128, 4)])
 def test_ln_projection(m, a, g, n, h):
   from colabfold_kernels import ops
   rng = np.random.default_rng(4)
