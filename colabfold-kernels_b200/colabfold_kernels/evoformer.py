@@ -71,7 +71,8 @@ def cuda_kernels():
       ln_projection=ops.ln_projection, packed_attention=ops.packed_attention_fwd, output_projection=ops.output_projection,
       opm_projection=ops.opm_projection, outer_product_mean=ops.outer_product_mean,
       opm_projection_cm=ops.opm_projection_cm, outer_product_mean_cm=ops.outer_product_mean_cm,
-      ln_gated_dual_proj=ops.ln_gated_dual_proj, contract=ops.contract, contract_gathered=ops.contract_gathered,
+      ln_gated_dual_proj=ops.ln_gated_dual_proj, ln_gated_dual_proj_peer=ops.ln_gated_dual_proj_peer,
+      contract=ops.contract, contract_gathered=ops.contract_gathered,
       contract_exchanged=ops.contract_exchanged,
       trimul_epilogue=ops.trimul_epilogue,
       transition=transition)
@@ -187,8 +188,24 @@ class PeerExchange:
       buf = self.symm.empty(nbytes, dtype=torch.uint8, device=self.device)
       h = self.symm.rendezvous(buf, self.group)
       self._handles.append(h)
-      self.sites[site] = (buf, torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=self.device))
+      host = [int(p) for p in h.buffer_ptrs]
+      self.sites[site] = (buf, torch.tensor(host, dtype=torch.int64, device=self.device), host)
     return self.sites[site]
+
+  def receive_buffer(self, site, shape, dtype):
+    """The site's receive buffer as a tensor of this shape, and every rank's address of it (for a kernel whose own
+    stores are the exchange, ops.ln_gated_dual_proj_peer); barrier() goes between those stores and the first read."""
+    nbytes = torch.empty((), dtype=dtype).element_size()
+    for d in shape:
+      nbytes *= d
+    buf, _, host = self._site(site, nbytes)
+    return buf[:nbytes].view(dtype).view(shape), host
+
+  def barrier(self):
+    """The flag barrier alone (bounded wait, code 1901): every rank's earlier kernels on this stream have completed."""
+    from colabfold_kernels import ops
+    ops.peer_alltoall(self.flags, self.flag_ptrs, self.flag_ptrs, self.counter, self.rank, self.P, rows=0, run_bytes=0,
+                      src_part=0, dst_part=0)
 
   def all_gather(self, site, x, dim):
     """Every rank's x concatenated along dim (0 or any later axis) -> a view of the site's receive buffer: each rank writes
@@ -200,7 +217,7 @@ class PeerExchange:
     for d in x.shape[:dim]:
       lead *= d
     run = x.numel() // lead * es          # bytes of one leading-index slice of the local shard
-    buf, ptrs = self._site(site, P * x.numel() * es)
+    buf, ptrs, _ = self._site(site, P * x.numel() * es)
     ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, P, rows=lead, run_bytes=run, src_part=0, src_row=run,
                       dst_part=run, dst_row=P * run)
     shape = list(x.shape)
@@ -213,7 +230,7 @@ class PeerExchange:
     out_shape the shape of what arrives."""
     from colabfold_kernels import ops
     nbytes = x.numel() * x.element_size()
-    buf, ptrs = self._site(site, nbytes)
+    buf, ptrs, _ = self._site(site, nbytes)
     ops.peer_alltoall(x, ptrs, self.flag_ptrs, self.counter, self.rank, self.P, **strides)
     return buf[:nbytes].view(x.dtype).view(x.shape if out_shape is None else out_shape)
 
@@ -321,6 +338,38 @@ class ShardedBlock:
     out = self.exchange(self.K.contract_exchanged(ap, bp, split_k=split_k))  # [P, c/P, rows/P, r] = [c, rows/P, r]
     return out.view(c, out.shape[2], out.shape[3])
 
+  def projected_triangle_product(self, pair_r, t, mask, incoming):
+    """triangle_product with the two operand all-to-alls done by the projection kernel's own stores
+    (ops.ln_gated_dual_proj_peer: channel part q of this rank's left and right go straight into rank q's receive
+    buffers over NVLink peer memory), then one flag barrier; None when that form does not apply (no peer exchange,
+    e4m3 operands, shard sizes outside the exchanged form)."""
+    P, K = self.P, self.K
+    a, b, c = pair_r.shape[0], pair_r.shape[1], 128
+    outer, inner = (b, a) if incoming else (a, b)
+    rows, k_local = (outer, inner) if incoming else (outer * P, inner)
+    unit = 128 // pair_r.element_size()
+    if self.peer is None or self.f8 or not hasattr(K, "ln_gated_dual_proj_peer") or not hasattr(K, "contract_exchanged"):
+      return None
+    if pair_r.shape[2] != 128 or t["wp"].shape[1] != 256 or pair_r.dtype != torch.bfloat16 or 16 % P or P > 8:
+      return None
+    if rows % (128 * P) or (incoming and k_local % unit) or (inner * pair_r.element_size()) % 16:
+      return None
+    # with the operands' exchange inside the projection's stores the exchanged form wins from two ranks on (8.11 against
+    # 8.26 ms for the gathered form at N_res 1024 on 2 GPUs)
+    if not self.exchange_triangle if self.exchange_triangle is not None else P < 2:
+      return None
+    shape = (P, c // P, outer, inner)
+    self._site_no += 1
+    lbuf, lptrs = self.peer.receive_buffer(self._site_no, shape, pair_r.dtype)
+    self._site_no += 1
+    rbuf, rptrs = self.peer.receive_buffer(self._site_no, shape, pair_r.dtype)
+    K.ln_gated_dual_proj_peer(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"], mask, lptrs, rptrs,
+                              self.rank, transpose=incoming)
+    self.peer.barrier()
+    ap, bp = (rbuf, lbuf) if incoming else (lbuf, rbuf)
+    out = self.exchange(K.contract_exchanged(ap, bp, split_k=incoming))
+    return out.view(c, out.shape[2], out.shape[3])
+
   def shard(self, n):
     step = n // self.P
     return slice(self.rank * step, (self.rank + 1) * step)
@@ -395,15 +444,20 @@ class ShardedBlock:
     msa_s = self.cols_to_rows(msa_c)
     # 5 triangle multiplication, outgoing edges: local rows of the left operand, all rows of the right
     t = prm["tri_out"]
-    l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
-                                 pair_mask[rs].contiguous().to(pair_r.dtype), **self.f8)
-    x_cm = self.triangle_product(l, rr, False)
-    pair_r = triangle_update(K, pair_r, x_cm if x_cm is not None else self.contract_all(l, rr), t)
+    x_cm = self.projected_triangle_product(pair_r, t, pair_mask[rs].contiguous().to(pair_r.dtype), False)
+    if x_cm is None:
+      l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
+                                   pair_mask[rs].contiguous().to(pair_r.dtype), **self.f8)
+      x_cm = self.triangle_product(l, rr, False)
+      if x_cm is None:
+        x_cm = self.contract_all(l, rr)
+    pair_r = triangle_update(K, pair_r, x_cm, t)
     # 6 incoming edges: out[i, j] = sum_k r[k, i] l[k, j].  Read transposed, this rank's pair rows give every (i, j)'s
     # operands for its own k: a slice of the contracted axis
     t = prm["tri_in"]
-    l, rr, x_cm = None, None, None
-    if r % (128 * self.P) == 0 and (self.exchange_triangle if self.exchange_triangle is not None else self.P >= 4):
+    l, rr = None, None
+    x_cm = self.projected_triangle_product(pair_r, t, pair_mask[rs].contiguous().to(pair_r.dtype), True)
+    if x_cm is None and r % (128 * self.P) == 0 and (self.exchange_triangle if self.exchange_triangle is not None else self.P >= 4):
       l, rr = K.ln_gated_dual_proj(pair_r, t["ln"][0], t["ln"][1], t["wp"], t["bp"], t["wg"], t["bg"],
                                    pair_mask[rs].contiguous().to(pair_r.dtype), transpose=True, **self.f8)
       x_cm = self.triangle_product(rr, l, True)

@@ -263,6 +263,24 @@ def ln_gated_dual_proj(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, eps=1e-5, t
   return left, right
 
 
+def ln_gated_dual_proj_peer(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, left_ptrs, right_ptrs, rank, eps=1e-5,
+                            transpose=False, pad=1):
+  """ln_gated_dual_proj of the pair x [a,b,128] (bf16, 128 + 128 channels out) whose stores are the all-to-all over
+  channels: left_ptrs / right_ptrs are lists of P device addresses (ints), entry q = rank q's receive buffer
+  [P, 128 / P, outer, inner']; this rank's channel part q lands at index `rank` of buffer q.  Nothing is returned: the
+  caller runs a barrier across the ranks (peer_alltoall with rows=0) before reading its own buffer."""
+  import ctypes
+  x = _c(x)
+  dt = x.dtype
+  parts = len(left_ptrs)
+  lp = (ctypes.c_void_p * parts)(*[int(v) for v in left_ptrs])
+  rp = (ctypes.c_void_p * parts)(*[int(v) for v in right_ptrs])
+  with torch.cuda.device(x.device):
+    _lib.call("cfk_ln_gated_dual_proj_peer", _ptr(x), _ptr(_f32(ln_scale)), _ptr(_f32(ln_offset)), _ptr(_c(wp.to(dt))),
+              _ptr(_c(bp.to(dt))), _ptr(_c(wg.to(dt))), _ptr(_c(bg.to(dt))), _ptr(_c(mask.to(dt))), lp, rp, int(rank), parts,
+              x.shape[0], x.shape[1], x.shape[2], wp.shape[1], int(transpose), int(pad), float(eps), _stream())
+
+
 def _keep(keep):
   """keep [M] (the rows that matter, transition.py:29-38) -> (contiguous tensor or None, dtype tag)."""
   if keep is None:

@@ -53,6 +53,16 @@ constexpr int kOffClsG = kOffTmemG + 16;
 constexpr int kSmemG = kOffClsG + kMaxTilesG + 1024;
 static_assert(kSmemG <= 232448, "shared memory budget");
 
+constexpr int kMaxPartsG = 8;
+// Where the two outputs go: one tensor map per part of the channel axis.  One part: the caller's [128, outer, inner']
+// arrays.  P parts (the row-sharded triangle multiplication, which wants channel shards next): part p is channels
+// [p * 128 / P, (p + 1) * 128 / P) and goes into rank p's receive buffer [P, 128 / P, outer, inner'] at this rank's
+// index - the all-to-all over channels happens in this kernel's stores, over NVLink peer memory, with no pass of its own.
+struct GdpOutMaps {
+  CUtensorMap l[kMaxPartsG];
+  CUtensorMap r[kMaxPartsG];
+};
+
 struct GdpParams {
   const float* ln_scale;
   const float* ln_offset;
@@ -62,13 +72,13 @@ struct GdpParams {
   int64_t outer, inner, inner_pad, stride_outer, stride_inner;  // strides in rows of x
   int64_t ntiles, tiles_per_outer;
   float eps;
+  int parts;                  // parts of the channel axis, each with its own output maps
   int* status;
 };
 
 __global__ void __launch_bounds__(kThreadsG, 1)
 ln_gdp128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wp,
-                 const __grid_constant__ CUtensorMap tm_wg, const __grid_constant__ CUtensorMap tm_l,
-                 const __grid_constant__ CUtensorMap tm_r, const GdpParams prm) {
+                 const __grid_constant__ CUtensorMap tm_wg, const __grid_constant__ GdpOutMaps om, const GdpParams prm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   {
@@ -107,8 +117,10 @@ ln_gdp128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_wp);
     tma_prefetch_desc(&tm_wg);
-    tma_prefetch_desc(&tm_l);
-    tma_prefetch_desc(&tm_r);
+    for (int q = 0; q < prm.parts; ++q) {
+      tma_prefetch_desc(&om.l[q]);
+      tma_prefetch_desc(&om.r[q]);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -218,11 +230,15 @@ ln_gdp128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
           ok = mbar_wait_deadline(&stg_full[grp], sc & 1);
           if (!ok) { report_timeout(prm.status, 1608); break; }
           if (inside) {
-            if (nst == 1) {
-              tma_store_3d(&tm_l, stage, r0 + grp * 64, o, 0);
-              tma_store_3d(&tm_r, stage, r0 + grp * 64, o, 0);
-            } else {
-              tma_store_3d(set ? &tm_r : &tm_l, stage, r0 + grp * 64, o, 0);
+            // part q: rows q * 128 / parts .. of the atom (a multiple of 8 lines, so the swizzle phase is the atom's)
+            const int part_bytes = (128 / prm.parts) * 128;
+            for (int q = 0; q < prm.parts; ++q) {
+              if (nst == 1) {
+                tma_store_3d(&om.l[q], stage + q * part_bytes, r0 + grp * 64, o, 0);
+                tma_store_3d(&om.r[q], stage + q * part_bytes, r0 + grp * 64, o, 0);
+              } else {
+                tma_store_3d(set ? &om.r[q] : &om.l[q], stage + q * part_bytes, r0 + grp * 64, o, 0);
+              }
             }
           }
           tma_commit_group();
@@ -434,15 +450,20 @@ ln_gdp128_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
 
 }  // namespace
 
-// x [outer, inner, 128] read with the given row strides, wp / wg [128, 256], left / right [128, outer, inner_pad] bf16.
+// x [outer, inner, 128] read with the given row strides, wp / wg [128, 256].  parts == 1: left_ptrs[0] / right_ptrs[0] are
+// left / right [128, outer, inner_pad] bf16.  parts == P > 1: left_ptrs[q] / right_ptrs[q] are rank q's receive buffers
+// [P, 128 / P, outer, inner_pad] (peer mappings for q != rank), and this rank's channel part q lands at index `rank` there.
 // Returns CFK_ERR_UNSUPPORTED for what the general engine should take instead.
 int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* wp, const void* bp,
-                     const void* wg, const void* bg, const void* mask, void* left, void* right, int64_t outer, int64_t inner,
-                     int64_t inner_pad, int64_t stride_outer, int64_t stride_inner, float eps, cudaStream_t st) {
+                     const void* wg, const void* bg, const void* mask, void* const* left_ptrs, void* const* right_ptrs,
+                     int rank, int parts, int64_t outer, int64_t inner, int64_t inner_pad, int64_t stride_outer,
+                     int64_t stride_inner, float eps, cudaStream_t st) {
   if ((inner_pad * 2) % 16 != 0 || outer > INT32_MAX || inner_pad > INT32_MAX) return CFK_ERR_UNSUPPORTED;
-  if (!aligned16(x) || !aligned16(wp) || !aligned16(wg) || !aligned16(left) || !aligned16(right) || !aligned16(ln_scale) ||
-      !aligned16(ln_offset))
+  if (parts < 1 || parts > kMaxPartsG || 128 % parts != 0 || (128 / parts) % 8 != 0 || rank < 0 || rank >= parts)
     return CFK_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(wp) || !aligned16(wg) || !aligned16(ln_scale) || !aligned16(ln_offset)) return CFK_ERR_UNSUPPORTED;
+  for (int q = 0; q < parts; ++q)
+    if (!left_ptrs[q] || !right_ptrs[q] || !aligned16(left_ptrs[q]) || !aligned16(right_ptrs[q])) return CFK_ERR_UNSUPPORTED;
   GdpParams prm{};
   prm.ln_scale = ln_scale; prm.ln_offset = ln_offset;
   prm.bp = static_cast<const __nv_bfloat16*>(bp); prm.bg = static_cast<const __nv_bfloat16*>(bg);
@@ -452,10 +473,12 @@ int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offse
   prm.tiles_per_outer = (inner_pad + kRowsG - 1) / kRowsG;
   prm.ntiles = outer * prm.tiles_per_outer;
   prm.eps = eps;
+  prm.parts = parts;
   prm.status = device_status_word();
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   if (prm.ntiles == 0) return CFK_OK;
-  CUtensorMap tx, twp, twg, tl, tr;
+  CUtensorMap tx, twp, twg;
+  GdpOutMaps om{};
   {
     const uint64_t row = uint64_t(kKc) * 2;
     uint64_t dims[3] = {uint64_t(kKc), uint64_t(inner), uint64_t(outer)};
@@ -471,13 +494,17 @@ int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offse
     int rc = make_tensor_map(i ? &twg : &twp, i ? wg : wp, CFK_BF16, 2, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
   }
-  for (int i = 0; i < 2; ++i) {
-    uint64_t dims[3] = {uint64_t(inner_pad), uint64_t(outer), 128};
-    uint64_t str[2] = {uint64_t(inner_pad) * 2, uint64_t(outer) * uint64_t(inner_pad) * 2};
-    uint32_t box[3] = {64, 1, 128};
-    int rc = make_tensor_map(i ? &tr : &tl, i ? right : left, CFK_BF16, 3, dims, str, box, 128);
-    if (rc != CFK_OK) return rc;
-  }
+  const int cpart = 128 / parts;
+  const uint64_t part_elems = uint64_t(cpart) * uint64_t(outer) * uint64_t(inner_pad);   // one rank's share of a buffer
+  for (int i = 0; i < 2; ++i)
+    for (int q = 0; q < parts; ++q) {
+      uint64_t dims[3] = {uint64_t(inner_pad), uint64_t(outer), uint64_t(cpart)};
+      uint64_t str[2] = {uint64_t(inner_pad) * 2, uint64_t(outer) * uint64_t(inner_pad) * 2};
+      uint32_t box[3] = {64, 1, uint32_t(cpart)};
+      char* base = static_cast<char*>(i ? right_ptrs[q] : left_ptrs[q]) + (parts > 1 ? uint64_t(rank) * part_elems * 2 : 0);
+      int rc = make_tensor_map(i ? &om.r[q] : &om.l[q], base, CFK_BF16, 3, dims, str, box, 128);
+      if (rc != CFK_OK) return rc;
+    }
   if (cudaFuncSetAttribute(ln_gdp128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemG) != cudaSuccess)
     return CFK_ERR_LAUNCH;
   int dev = 0, sms = 148;
@@ -485,7 +512,7 @@ int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offse
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = int(prm.ntiles < sms ? prm.ntiles : sms);
   if ((prm.ntiles + grid - 1) / grid > kMaxTilesG) return CFK_ERR_UNSUPPORTED;
-  ln_gdp128_kernel<<<grid, kThreadsG, kSmemG, st>>>(tx, twp, twg, tl, tr, prm);
+  ln_gdp128_kernel<<<grid, kThreadsG, kSmemG, st>>>(tx, twp, twg, om, prm);
   return check_launch();
 }
 

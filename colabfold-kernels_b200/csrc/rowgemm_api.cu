@@ -101,7 +101,7 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   prm.inner_pad = (prm.inner + pad - 1) / pad * pad;
   prm.eps = eps;
   if (k == 128 && p == 256 && !fp8) {  // the triangle multiplication's shape has a kernel of its own
-    const int rc = ln_gdp128_launch(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, left, right, prm.outer, prm.inner,
+    const int rc = ln_gdp128_launch(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, &left, &right, 0, 1, prm.outer, prm.inner,
                                     prm.inner_pad, prm.src[0].stride_outer, prm.src[0].stride_inner, eps,
                                     static_cast<cudaStream_t>(stream));
     if (rc != CFK_ERR_UNSUPPORTED) return rc;
@@ -119,6 +119,19 @@ extern "C" int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, cons
   // the mask doubles as the row-block filter: a tile of zeros skips the work, a tile below zero is left unwritten
   prm.keep = mask; prm.keep_dtype = CFK_BF16;
   return run_chunks(prm, 2 * cpa, wp, wg, 1, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cfk_ln_gated_dual_proj_peer(const void* x, const float* ln_scale, const float* ln_offset, const void* wp,
+                                           const void* bp, const void* wg, const void* bg, const void* mask,
+                                           void* const* left_ptrs, void* const* right_ptrs, int rank, int parts, int64_t a,
+                                           int64_t b, int k, int p, int transpose, int pad, float eps, void* stream) {
+  if (!x || !ln_scale || !ln_offset || !wp || !bp || !wg || !bg || !mask || !left_ptrs || !right_ptrs) return CFK_ERR_NULL;
+  if (a <= 0 || b <= 0 || pad < 1 || parts < 1 || rank < 0 || rank >= parts) return CFK_ERR_SHAPE;
+  if (k != 128 || p != 256) return CFK_ERR_UNSUPPORTED;
+  const int64_t outer = transpose ? b : a, inner = transpose ? a : b;
+  const int64_t inner_pad = (inner + pad - 1) / pad * pad;
+  return ln_gdp128_launch(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, left_ptrs, right_ptrs, rank, parts, outer, inner,
+                          inner_pad, transpose ? 1 : b, transpose ? b : 1, eps, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cfk_trimul_epilogue(const void* x_cm, int x_cm_dtype, const void* act, const float* in_scale,

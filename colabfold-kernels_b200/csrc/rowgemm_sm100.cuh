@@ -90,8 +90,9 @@ int ln_proj128_launch(const void* x, const float* ln_scale, const float* ln_offs
 // LayerNorm -> gated dual projection at 128 channels in and 128 + 128 out, channel-major bf16 (ln_gdp128_sm100.cu);
 // returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.
 int ln_gdp128_launch(const void* x, const float* ln_scale, const float* ln_offset, const void* wp, const void* bp,
-                     const void* wg, const void* bg, const void* mask, void* left, void* right, int64_t outer, int64_t inner,
-                     int64_t inner_pad, int64_t stride_outer, int64_t stride_inner, float eps, cudaStream_t st);
+                     const void* wg, const void* bg, const void* mask, void* const* left_ptrs, void* const* right_ptrs,
+                     int rank, int parts, int64_t outer, int64_t inner, int64_t inner_pad, int64_t stride_outer,
+                     int64_t stride_inner, float eps, cudaStream_t st);
 
 // Triangle-multiplication output at 128 channels with LayerNorm folded around the GEMMs (trimul_epi128_sm100.cu);
 // returns CFK_ERR_UNSUPPORTED for shapes the general engine should take.

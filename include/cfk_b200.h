@@ -215,6 +215,20 @@ CFK_API int cfk_ln_gated_dual_proj(const void* x, const float* ln_scale, const f
                                    void* right, int64_t a, int64_t b, int k, int p, int transpose, int pad, int fp8,
                                    float fp8_scale, float eps, void* stream);
 
+/* The same projection (bf16, k = 128, p = 256, pair x [a,b,k]) with the all-to-all over channels of the row-sharded
+ * triangle multiplication done by its stores: left_ptrs / right_ptrs are HOST arrays of `parts` device pointers,
+ * entry q = rank q's receive buffer [parts, 128 / parts, outer, inner'] (this rank's own buffer for q == rank, NVLink
+ * peer mappings otherwise); channel part q of this rank's result lands at index `rank` of buffer q (TMA stores, no
+ * multicast).  parts divides 16, parts <= 8.  The caller orders the exchange: a barrier across the ranks
+ * (cfk_peer_alltoall with rows == 0) after this call and before any rank reads its buffer, and one between the last
+ * read of a buffer and the next call that writes it.  parts == 1 is cfk_ln_gated_dual_proj with left_ptrs[0],
+ * right_ptrs[0].  CFK_ERR_UNSUPPORTED for other shapes.
+ * Replaces ln_gated_dual_proj, tri_mul.py:222-283, followed by the exchange the reference (one device) does not need. */
+CFK_API int cfk_ln_gated_dual_proj_peer(const void* x, const float* ln_scale, const float* ln_offset, const void* wp,
+                                        const void* bp, const void* wg, const void* bg, const void* mask,
+                                        void* const* left_ptrs, void* const* right_ptrs, int rank, int parts, int64_t a,
+                                        int64_t b, int k, int p, int transpose, int pad, float eps, void* stream);
+
 /* Triangle-multiplication output: out = (LN(x_cm^T) wo + bo) * sigmoid(g wg + bg) (+ residual | + act).
  * x_cm [c,m] channel-major product (x_cm_dtype CFK_BF16 or CFK_F32); act [m,ca] is the gate input: already normed
  * when in_scale == NULL, else the raw module input normed here with in_scale/in_offset; add_input adds act itself

@@ -75,3 +75,35 @@ def test_missing_peer_times_out_instead_of_hanging():
     ops.layer_norm(send, torch.ones(1024, device="cuda"), torch.zeros(1024, device="cuda"))
   assert ops.device_status() == 1901 and ops.device_status() == 0
   ops.layer_norm(send, torch.ones(1024, device="cuda"), torch.zeros(1024, device="cuda"))
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+@pytest.mark.parametrize("transpose", [False, True])
+def test_projection_whose_stores_are_the_exchange(P, transpose):
+  """ops.ln_gated_dual_proj_peer with the ranks emulated in turn on one GPU (every "peer" buffer is a local one):
+  channel part q of rank r's left / right must land at index r of buffer q, bit-identical to the same kernel's
+  ordinary outputs (the all-to-all over channels of the row-sharded triangle multiplication, evoformer.py
+  ShardedBlock.projected_triangle_product; tri_mul.py:222-283 for the projection itself)."""
+  from colabfold_kernels import ops
+  g = torch.Generator().manual_seed(7 * P + int(transpose))
+  a, b, k, p = (40, 256, 128, 256) if not transpose else (64, 136, 128, 256)
+  rn = lambda *s, sc=1.0: (torch.randn(*s, generator=g) * sc).to(bf).cuda()
+  wp, bp_, wg, bg = rn(k, p, sc=k ** -.5), rn(p, sc=.1), rn(k, p, sc=k ** -.5), rn(p, sc=.1)
+  scale, offset = (1 + 0.1 * torch.randn(k, generator=g)).cuda(), (0.1 * torch.randn(k, generator=g)).cuda()
+  outer, inner = (b, a) if transpose else (a, b)
+  cp = 128 // P
+  lbufs = [torch.zeros(P, cp, outer, inner, dtype=bf, device="cuda") for _ in range(P)]
+  rbufs = [torch.zeros(P, cp, outer, inner, dtype=bf, device="cuda") for _ in range(P)]
+  want = []
+  for r in range(P):
+    x = rn(a, b, k)
+    mask = (torch.rand(a, b, generator=g) > .1).to(bf).cuda()
+    want.append(ops.ln_gated_dual_proj(x, scale, offset, wp, bp_, wg, bg, mask, transpose=transpose))
+    ops.ln_gated_dual_proj_peer(x, scale, offset, wp, bp_, wg, bg, mask, [t.data_ptr() for t in lbufs],
+                                [t.data_ptr() for t in rbufs], r, transpose=transpose)
+  torch.cuda.synchronize()
+  assert ops.device_status() == 0
+  for q in range(P):
+    for r in range(P):
+      assert torch.equal(lbufs[q][r], want[r][0][q * cp:(q + 1) * cp])
+      assert torch.equal(rbufs[q][r], want[r][1][q * cp:(q + 1) * cp])
