@@ -73,7 +73,7 @@ def cuda_kernels():
       opm_projection_cm=ops.opm_projection_cm, outer_product_mean_cm=ops.outer_product_mean_cm,
       ln_gated_dual_proj=ops.ln_gated_dual_proj, ln_gated_dual_proj_peer=ops.ln_gated_dual_proj_peer,
       contract=ops.contract, contract_gathered=ops.contract_gathered,
-      contract_exchanged=ops.contract_exchanged,
+      contract_exchanged=ops.contract_exchanged, contract_exchanged_peer=ops.contract_exchanged_peer,
       trimul_epilogue=ops.trimul_epilogue,
       transition=transition)
 
@@ -367,7 +367,13 @@ class ShardedBlock:
                               self.rank, transpose=incoming)
     self.peer.barrier()
     ap, bp = (rbuf, lbuf) if incoming else (lbuf, rbuf)
-    out = self.exchange(K.contract_exchanged(ap, bp, split_k=incoming))
+    if hasattr(K, "contract_exchanged_peer"):  # the product's way back likewise: stores into the peers' buffers, a barrier
+      self._site_no += 1
+      out, optrs = self.peer.receive_buffer(self._site_no, (P, c // P, rows // P, rows), pair_r.dtype)
+      K.contract_exchanged_peer(ap, bp, optrs, self.rank, split_k=incoming)
+      self.peer.barrier()
+    else:
+      out = self.exchange(K.contract_exchanged(ap, bp, split_k=incoming))
     return out.view(c, out.shape[2], out.shape[3])
 
   def shard(self, n):

@@ -214,6 +214,23 @@ def contract_exchanged(a_parts, b_parts, split_k=False, alpha=1.0, out=None):
   return out
 
 
+def contract_exchanged_peer(a_parts, b_parts, out_ptrs, rank, split_k=False, alpha=1.0):
+  """contract_exchanged whose stores are the all-to-all back to row shards: out_ptrs is a list of P device addresses
+  (ints), entry q = rank q's receive buffer [P, c, i/P, j] bf16; rows of part q land at index `rank` of buffer q.  The
+  caller runs a barrier across the ranks before reading its own buffer."""
+  import ctypes
+  a_parts, b_parts = _c(a_parts), _c(b_parts)
+  parts, c = a_parts.shape[0], a_parts.shape[1]
+  if split_k:
+    i, j, k = a_parts.shape[2], b_parts.shape[2], a_parts.shape[3] * parts
+  else:
+    i, j, k = a_parts.shape[2] * parts, b_parts.shape[2] * parts, a_parts.shape[3]
+  op = (ctypes.c_void_p * parts)(*[int(v) for v in out_ptrs])
+  with torch.cuda.device(a_parts.device):
+    _lib.call("cfk_contract_exchanged_peer", _ptr(a_parts), _ptr(b_parts), op, int(rank), c, i, j, k, tag(a_parts.dtype),
+              float(alpha), parts, int(split_k), _stream())
+
+
 # ------------------------------------------------------------------------------------------ projection family
 def _f32(t):
   return _c(t.float())

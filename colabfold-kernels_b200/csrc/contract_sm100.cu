@@ -40,11 +40,21 @@ struct ContractParams {
   // (a multiple of 128); 2: split along K, [parts, C, rows, K / parts] with `div` elements per part (a multiple of
   // the 128-byte slice).  The product only takes modes 0 and 1.
   int a_mode, a_div, b_mode, b_div, o_div;
+  int o_peer;           // > 0: part q of the product (rows [q o_div, (q + 1) o_div)) is stored through peer map q
+};
+
+// The exchanged form's product with the all-to-all back to row shards done by the stores: one 3-D map {J, o_div, C} per
+// destination rank, based at this rank's index of that rank's receive buffer [parts, C, o_div, J] (NVLink peer memory
+// for the other ranks; plain TMA stores, no multicast).
+constexpr int kMaxPeerParts = 8;
+struct ContractPeerMaps {
+  CUtensorMap o[kMaxPeerParts];
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
 contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                const __grid_constant__ CUtensorMap tm_o, const ContractParams prm) {
+                const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ ContractPeerMaps pm,
+                const ContractParams prm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   {
@@ -78,6 +88,7 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_o);
+    for (int q = 0; q < prm.o_peer; ++q) tma_prefetch_desc(&pm.o[q]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -204,6 +215,10 @@ contract_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 #pragma unroll
             for (int sub = 0; sub < 4; ++sub)
               tma_store_4d(&tm_o, stage + sub * (kTM * 64), 0, 0, (j0 + half * 128) / 32 + sub, i0 / 32);
+          } else if (prm.o_peer > 0) {
+            const CUtensorMap* m = &pm.o[i0 / prm.o_div];
+            tma_store_3d(m, stage, j0 + half * 128, i0 % prm.o_div, c);
+            tma_store_3d(m, stage + kTM * 128, j0 + half * 128 + 64, i0 % prm.o_div, c);
           } else if (prm.o_div > 0) {
             tma_store_4d(&tm_o, stage, j0 + half * 128, i0 % prm.o_div, c, i0 / prm.o_div);
             tma_store_4d(&tm_o, stage + kTM * 128, j0 + half * 128 + 64, i0 % prm.o_div, c, i0 / prm.o_div);
@@ -239,7 +254,14 @@ namespace {
 // xmode / xparts (exchanged form): mode 1 = operands split by rows over xparts, mode 2 = split along K; the product
 // is then stored split by rows, [xparts, C, I / xparts, J]
 int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype, float alpha, int opm_ri,
-                  int opm_rj, int parts, void* stream, int xmode = 0, int xparts = 1) {
+                  int opm_rj, int parts, void* stream, int xmode = 0, int xparts = 1, void* const* out_ptrs = nullptr,
+                  int rank = 0) {
+  if (out_ptrs != nullptr) {
+    if (xmode == 0 || xparts > kMaxPeerParts || rank < 0 || rank >= xparts) return CFK_ERR_UNSUPPORTED;
+    for (int q = 0; q < xparts; ++q)
+      if (out_ptrs[q] == nullptr || !aligned16(out_ptrs[q])) return CFK_ERR_ALIGN;
+    out = out_ptrs[rank];   // the 4-D map below is built but not used
+  }
   if (a == nullptr || b == nullptr || out == nullptr) return CFK_ERR_NULL;
   if (c <= 0 || i <= 0 || j <= 0 || k <= 0) return CFK_ERR_SHAPE;
   if (dtype != CFK_BF16 && dtype != CFK_E4M3) return CFK_ERR_DTYPE;
@@ -248,6 +270,7 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
   if ((int64_t(k) * es) % 16 != 0 || j % 8 != 0) return CFK_ERR_SHAPE;
   if (!aligned16(a) || !aligned16(b) || !aligned16(out)) return CFK_ERR_ALIGN;
   CUtensorMap ta, tb, to;
+  ContractPeerMaps pm{};
   int a_div = 0, b_div = 0, o_div = 0, part_rows = 0;
   if (xmode != 0) {
     const int kps = 128 / es;
@@ -278,6 +301,16 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
     uint32_t box[4] = {64, kTM, 1, 1};
     rc = make_tensor_map(&to, out, CFK_BF16, 4, dims, str, box, 128);
     if (rc != CFK_OK) return rc;
+    if (out_ptrs != nullptr) {
+      const uint64_t share = uint64_t(c) * o_div * j * 2;   // bytes one source rank fills of a receive buffer
+      for (int q = 0; q < xparts; ++q) {
+        uint64_t d3[3] = {uint64_t(j), uint64_t(o_div), uint64_t(c)};
+        uint64_t s3[2] = {uint64_t(j) * 2, uint64_t(o_div) * j * 2};
+        uint32_t b3[3] = {64, kTM, 1};
+        rc = make_tensor_map(&pm.o[q], static_cast<char*>(out_ptrs[q]) + uint64_t(rank) * share, CFK_BF16, 3, d3, s3, b3, 128);
+        if (rc != CFK_OK) return rc;
+      }
+    }
   } else {
   {
     uint64_t dims[3] = {uint64_t(k), uint64_t(i), uint64_t(c)};
@@ -320,7 +353,8 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
   }
   // exchanged form: the b boxes of mode 1 go through the gathered operand's path (two 128-row boxes, part = row / div)
   ContractParams prm{c, i, j, k, 128 / es, dtype == CFK_E4M3, alpha, device_status_word(), opm_ri > 0,
-                     xmode == 1 ? b_div : part_rows, xmode, a_div, xmode == 2 ? 2 : 0, b_div, o_div};
+                     xmode == 1 ? b_div : part_rows, xmode, a_div, xmode == 2 ? 2 : 0, b_div, o_div,
+                     out_ptrs != nullptr ? xparts : 0};
   if (prm.status == nullptr) return CFK_ERR_LAUNCH;
   // a function attribute belongs to the current device: set on every launch, as the other launchers do
   if (cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
@@ -330,7 +364,7 @@ int contract_impl(const void* a, const void* b, void* out, int c, int i, int j, 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t ntiles = int64_t(c) * ((i + kTM - 1) / kTM) * ((j + kTN - 1) / kTN);
   const int grid = int(ntiles < sms ? ntiles : sms);
-  contract_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(ta, tb, to, prm);
+  contract_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(ta, tb, to, pm, prm);
   return check_launch();
 }
 }  // namespace
@@ -350,6 +384,13 @@ extern "C" int cfk_contract_exchanged(const void* a, const void* b, void* out, i
                                       float alpha, int parts, int split_k, void* stream) {
   if (parts <= 0) return CFK_ERR_SHAPE;
   return contract_impl(a, b, out, c, i, j, k, dtype, alpha, 0, 0, 1, stream, split_k ? 2 : 1, parts);
+}
+
+extern "C" int cfk_contract_exchanged_peer(const void* a, const void* b, void* const* out_ptrs, int rank, int c, int i, int j,
+                                           int k, int dtype, float alpha, int parts, int split_k, void* stream) {
+  if (parts <= 0) return CFK_ERR_SHAPE;
+  if (out_ptrs == nullptr) return CFK_ERR_NULL;
+  return contract_impl(a, b, nullptr, c, i, j, k, dtype, alpha, 0, 0, 1, stream, split_k ? 2 : 1, parts, out_ptrs, rank);
 }
 
 extern "C" int cfk_opm_outer_product(const void* a, const void* b, void* out, int ri, int rj, int s, int dtype, void* stream) {

@@ -168,6 +168,14 @@ CFK_API int cfk_contract_gathered(const void* a, const void* b, void* out, int c
 CFK_API int cfk_contract_exchanged(const void* a, const void* b, void* out, int c, int i, int j, int k, int dtype,
                                    float alpha, int parts, int split_k, void* stream);
 
+/* cfk_contract_exchanged with the all-to-all of the product back to row shards done by its stores: out_ptrs is a HOST
+ * array of `parts` device pointers, entry q = rank q's receive buffer [parts, c, i / parts, j] bf16 (this rank's own for
+ * q == rank, NVLink peer mappings otherwise); rows [q i/parts, (q+1) i/parts) of this rank's product land at index
+ * `rank` of buffer q (TMA stores, no multicast).  parts <= 8.  The caller orders the exchange as for
+ * cfk_ln_gated_dual_proj_peer: a barrier across the ranks after this call and before any rank reads its buffer. */
+CFK_API int cfk_contract_exchanged_peer(const void* a, const void* b, void* const* out_ptrs, int rank, int c, int i, int j,
+                                        int k, int dtype, float alpha, int parts, int split_k, void* stream);
+
 /* All-to-all over NVLink peer memory for the row-sharded block (one process per GPU): part p of `send` is written into
  * rank p's receive buffer by plain 16-byte stores of a kernel of this library (no TMA, no multicast), followed by a flag
  * barrier after which every rank's receive buffer holds all parts.  A part is `rows` runs of run_bytes: run i of part p

@@ -107,3 +107,26 @@ def test_projection_whose_stores_are_the_exchange(P, transpose):
     for r in range(P):
       assert torch.equal(lbufs[q][r], want[r][0][q * cp:(q + 1) * cp])
       assert torch.equal(rbufs[q][r], want[r][1][q * cp:(q + 1) * cp])
+
+
+@pytest.mark.parametrize("P", [2, 4])
+@pytest.mark.parametrize("split_k", [False, True])
+def test_contraction_whose_stores_are_the_exchange(P, split_k):
+  """ops.contract_exchanged_peer with the ranks emulated in turn on one GPU: rows [q i/P, (q+1) i/P) of rank r's
+  product must land at index r of buffer q, bit-identical to ops.contract_exchanged's send buffer (the all-to-all of
+  the triangle product back to row shards, evoformer.py ShardedBlock.projected_triangle_product)."""
+  from colabfold_kernels import ops
+  g = torch.Generator().manual_seed(11 * P + int(split_k))
+  c, n, k = 3, 128 * P, 64 * P
+  shape = (P, c, n, k // P) if split_k else (P, c, n // P, k)
+  obufs = [torch.zeros(P, c, n // P, n, dtype=bf, device="cuda") for _ in range(P)]
+  want = []
+  for r in range(P):
+    a, b = torch.randn(shape, generator=g).to(bf).cuda(), torch.randn(shape, generator=g).to(bf).cuda()
+    want.append(ops.contract_exchanged(a, b, split_k=split_k))
+    ops.contract_exchanged_peer(a, b, [t.data_ptr() for t in obufs], r, split_k=split_k)
+  torch.cuda.synchronize()
+  assert ops.device_status() == 0
+  for q in range(P):
+    for r in range(P):
+      assert torch.equal(obufs[q][r], want[r][q])
