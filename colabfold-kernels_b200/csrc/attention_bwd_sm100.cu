@@ -217,7 +217,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (lane == 0) {
         constexpr uint32_t idesc_s = make_idesc(kBQ, kBK, 1, 1, 0, 0);   // S, dP: both operands K-major
         constexpr uint32_t idesc_t = make_idesc(kBK, D, 1, 1, 1, 1);     // dV, dK: A = P^T / dS^T (MN-major), B MN-major
-        constexpr uint32_t idesc_q = make_idesc(kBQ, D, 1, 1, 0, 1);     // dQ: A = dS (K-major), B = K (MN-major)
         constexpr uint32_t kTile16 = kTile >> 4;
         // low descriptor words (start address >> 4, leading byte offset); the high words are constants
         constexpr uint32_t hi64 = desc_hi(8 * kRowBytes, kSwz64);   // Q, dO, K, V tiles: 64-byte rows
@@ -253,7 +252,6 @@ attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           if (!mbar_wait_deadline(pds_full, pf_par)) { report_timeout(prm.status, 704); return false; }
           tc_fence_after();
           const uint32_t bdo = do_mn + o_st * kTile16, bq = q_mn + o_st * kTile16;
-          const uint32_t bk = k_mn + o_g * kTile16;
           const uint32_t d_k = tmem + kColAcc + o_g * 64, d_v = d_k + 32;
           const uint32_t acc0 = o_first ^ 1;  // the first query block overwrites the dK/dV accumulators
           // dV_g += P^T dO and dK_g += dS^T Q: A MN-major, a K step is 16 query rows = 2048 bytes of P/dS,
