@@ -350,7 +350,9 @@ class ShardedBlock:
     unit = 128 // pair_r.element_size()
     if self.peer is None or self.f8 or not hasattr(K, "ln_gated_dual_proj_peer") or not hasattr(K, "contract_exchanged"):
       return None
-    if pair_r.shape[2] != 128 or t["wp"].shape[1] != 256 or pair_r.dtype != torch.bfloat16 or 16 % P or P > 8:
+    if pair_r.shape[2] != 128 or t["wp"].shape[1] != 256 or 16 % P or P > 8:
+      return None
+    if pair_r.dtype not in getattr(K.ln_gated_dual_proj_peer, "dtypes", (pair_r.dtype,)):  # the CUDA kernel: bf16 only
       return None
     if rows % (128 * P) or (incoming and k_local % unit) or (inner * pair_r.element_size()) % 16:
       return None

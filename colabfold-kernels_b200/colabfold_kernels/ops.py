@@ -298,6 +298,9 @@ def ln_gated_dual_proj_peer(x, ln_scale, ln_offset, wp, bp, wg, bg, mask, left_p
               x.shape[0], x.shape[1], x.shape[2], wp.shape[1], int(transpose), int(pad), float(eps), _stream())
 
 
+ln_gated_dual_proj_peer.dtypes = (torch.bfloat16,)
+
+
 def _keep(keep):
   """keep [M] (the rows that matter, transition.py:29-38) -> (contiguous tensor or None, dtype tag)."""
   if keep is None:

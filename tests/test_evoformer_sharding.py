@@ -56,6 +56,88 @@ def test_two_rank_block_matches_single_device(tmp_path, s_r):
   assert float((p - ref_p).abs().max()) <= 1e-4 * float(ref_p.abs().max())
 
 
+class _FakePeer:
+  """Stands in for evoformer.PeerExchange on CPU: the receive buffers are local tensors, the "addresses" handed to the
+  kernels are the site numbers (every rank names a site the same way), the barrier is the process group's."""
+
+  def __init__(self, world):
+    self.P, self.bufs = world, {}
+
+  def receive_buffer(self, site, shape, dtype):
+    self.bufs[site] = torch.empty(shape, dtype=dtype)
+    return self.bufs[site], [site] * self.P
+
+  def barrier(self):
+    dist.barrier()
+
+
+def _fused_worker(rank, world, port, out):
+  """The block with the triangle multiplication's exchanges done by the producing kernels' stores
+  (ShardedBlock.projected_triangle_product): the two "peer" kernels are emulated by the oracle's kernels followed by the
+  all-to-all that their stores amount to, so the wiring (buffer shapes, operand roles of the incoming update, site
+  numbering, barriers) runs on CPU."""
+  for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
+    sys.path.insert(0, p)
+  import types
+  from colabfold_kernels import evoformer
+  from oracle.evoformer_ref import oracle_kernels
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  dist.init_process_group("gloo", rank=rank, world_size=world)
+  torch.set_num_threads(2)
+  K0, fake, calls = oracle_kernels(), _FakePeer(world), []
+
+  def ln_gated_dual_proj_peer(x, sc, of, wp, bp, wg, bg, mask, lptrs, rptrs, my_rank, transpose=False):
+    assert my_rank == rank and len(lptrs) == world
+    l, r = K0.ln_gated_dual_proj(x, sc, of, wp, bp, wg, bg, mask, transpose=transpose)
+    for t, site in ((l, lptrs[0]), (r, rptrs[0])):
+      send = t.reshape((world, t.shape[0] // world) + tuple(t.shape[1:])).contiguous()
+      assert tuple(fake.bufs[site].shape) == tuple(send.shape)
+      dist.all_to_all_single(fake.bufs[site], send)
+    calls.append("projection")
+
+  def contract_exchanged_peer(ap, bp, optrs, my_rank, split_k=False):
+    send = K0.contract_exchanged(ap, bp, split_k=split_k).contiguous()
+    assert tuple(fake.bufs[optrs[0]].shape) == tuple(send.shape)
+    dist.all_to_all_single(fake.bufs[optrs[0]], send)
+    calls.append("contraction")
+
+  K = types.SimpleNamespace(**vars(K0), ln_gated_dual_proj_peer=ln_gated_dual_proj_peer,
+                            contract_exchanged_peer=contract_exchanged_peer)
+  msa, pair, msa_mask, pair_mask = _inputs(4, 256)
+  params = evoformer.init_params(dtype=torch.float32, seed=1)
+  blk = evoformer.ShardedBlock(K, params)
+  inner = blk.projected_triangle_product
+
+  def with_peer(*a, **k):  # only this step sees the peer exchange: every other collective stays on the process group
+    blk.peer = fake
+    try:
+      return inner(*a, **k)
+    finally:
+      blk.peer = None
+
+  blk.projected_triangle_product = with_peer
+  m, p = blk(msa[blk.shard(4)].contiguous(), pair[blk.shard(256)].contiguous(), msa_mask, pair_mask)
+  torch.save((m, p, calls), os.path.join(out, f"rank{rank}.pt"))
+  dist.destroy_process_group()
+
+
+@pytest.mark.timeout(900)
+def test_two_rank_block_with_the_exchanges_in_the_kernels_stores(tmp_path):
+  from colabfold_kernels import evoformer
+  from oracle.evoformer_ref import oracle_kernels
+  world, port = 2, 29011 + os.getpid() % 200
+  mp.spawn(_fused_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+  msa, pair, msa_mask, pair_mask = _inputs(4, 256)
+  params = evoformer.init_params(dtype=torch.float32, seed=1)
+  ref_m, ref_p = evoformer.block(oracle_kernels(), msa, pair, msa_mask, pair_mask, params)
+  got = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(world)]
+  assert all(g[2] == ["projection", "contraction"] * 2 for g in got)  # outgoing and incoming update, both fused
+  m = torch.cat([g[0] for g in got], 0)
+  p = torch.cat([g[1] for g in got], 0)
+  assert float((m - ref_m).abs().max()) <= 1e-4 * float(ref_m.abs().max())
+  assert float((p - ref_p).abs().max()) <= 1e-4 * float(ref_p.abs().max())
+
+
 def _bad_shard_worker(rank, world, port, out):
   for p in (ROOT, os.path.join(ROOT, "colabfold-kernels_b200")):
     sys.path.insert(0, p)
