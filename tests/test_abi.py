@@ -24,6 +24,10 @@ def test_bad_arguments_return_status_without_a_gpu():
   assert lib.cfk_layer_norm(None, None, None, None, 4, 8, _lib.BF16, 1e-5, None) == -4   # CFK_ERR_NULL
   assert lib.cfk_attention_fwd(None, None, None, None, None, None, None, 1, 1, 1, 1, 1, _lib.BF16, 0, 1.0, None) == -4
   assert lib.cfk_trim_limits(None, None, 1, 1, None) == -4
+  # the entries whose stores are the exchange of the row-sharded triangle multiplication: null arrays of peer pointers
+  assert lib.cfk_ln_gated_dual_proj_peer(None, None, None, None, None, None, None, None, None, None, 0, 2, 128, 128, 128, 256,
+                                         0, 1, 1e-5, None) == -4
+  assert lib.cfk_contract_exchanged_peer(None, None, None, 0, 64, 256, 256, 256, _lib.BF16, 1.0, 2, 0, None) == -4
 
 
 def test_cpu_tensors_are_refused():
